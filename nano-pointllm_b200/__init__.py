@@ -1,0 +1,21 @@
+"""nanopointllm_b200: B200-native (sm_100a) W8A8 linear + paged-decode path.
+
+The directory is named ``nano-pointllm_b200`` and is imported under the module
+name ``nanopointllm_b200`` (the entry points register it with importlib).
+
+Public surface, mirroring the reference ``nanopointllm`` API for this path:
+
+* ``nanopointllm_b200.w8a8``            - the W8A8 contract on the GPU
+  (quantize_symmetric, scale_from_absmax, per_output_weight_quant,
+  dynamic_per_token_quant, integer_linear_per_output, W8A8Linear)
+* ``nanopointllm_b200.paged_attention`` - store_kvcache, paged_decode_attention,
+  rope_store_kvcache
+* ``nanopointllm_b200.runner``          - W8A8 Llama decode runner
+  (inject/quantize a model, prefill + decode steps, CUDA-graph decode)
+
+Every compute call goes through the C-ABI library ``libnpl_w8a8.so`` built
+from ``csrc/``; there is no CPU or library fallback.
+"""
+from __future__ import annotations
+
+__all__ = ["w8a8", "paged_attention", "runner", "synthetic"]

@@ -1,0 +1,334 @@
+"""Generate the golden fixtures in tests/golden/ by running the REFERENCE.
+
+Run in a container where the reference project is importable, e.g.
+
+    NPL_REFERENCE=/path/to/Nano-pointllm python tests/golden/make_golden.py
+
+Each fixture records inputs (or the seeded recipe that rebuilds them) together
+with the reference's own outputs. The tests then pin the numpy oracle and the
+CUDA kernels to these outputs without needing the reference at run time.
+
+Reference entry points used (paths relative to the reference root):
+  nanopointllm/compression/w8a8.py      quantize_symmetric, scale_from_absmax,
+                                         per_output_weight_qdq,
+                                         dynamic_per_token_activation_qdq,
+                                         integer_linear_per_output_reference
+  nanopointllm/llama/lightweight_runner.py  LightweightRMSNorm, LightweightLlamaRunner
+  nanopointllm/llama/paged_attention.py     store_kvcache, _paged_decode_attention_pytorch
+  nanopointllm/llama/inject_paged.py        inject_paged_attention
+  nanopointllm/engine/kv_pool.py            allocate_kv_pool
+  transformers (installed 5.5.0)            LlamaRotaryEmbedding, apply_rotary_pos_emb
+"""
+from __future__ import annotations
+
+import hashlib
+import importlib.util
+import json
+import os
+import pathlib
+import sys
+
+import numpy as np
+import torch
+
+HERE = pathlib.Path(__file__).resolve().parent
+REPO = HERE.parent.parent
+REF = pathlib.Path(os.environ.get("NPL_REFERENCE", "/root/reference"))
+
+
+def _import_repo():
+    sys.path.insert(0, str(REPO))
+    pkg = REPO / "nano-pointllm_b200"
+    spec = importlib.util.spec_from_file_location(
+        "nanopointllm_b200", pkg / "__init__.py", submodule_search_locations=[str(pkg)])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules["nanopointllm_b200"] = mod
+    spec.loader.exec_module(mod)
+
+
+def sha(a: np.ndarray) -> str:
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+def f16(t: torch.Tensor) -> np.ndarray:
+    return t.detach().to(torch.float16).numpy()
+
+
+def main() -> None:
+    sys.path.insert(0, str(REF))
+    os.environ.setdefault("PYTHONDONTWRITEBYTECODE", "1")
+    _import_repo()
+    from nanopointllm.compression import w8a8 as R
+    from nanopointllm_b200 import synthetic as S
+
+    torch.set_num_threads(max(1, os.cpu_count() or 1))
+
+    # 1. Rounding/clipping KAT: the reference's own vector (tests/test_w8a8_contract.py:15-21).
+    kat_in = torch.tensor([-200.0, -127.5, -2.5, -1.5, 1.5, 2.5, 127.5, 200.0])
+    kat_out = R.quantize_symmetric(kat_in, torch.tensor(1.0))
+    # Int golden of the quantized-package test (tests/test_quantized_tensor_package.py:11-39).
+    pkg_a = np.array([[1, -2, 3, -4], [5, 6, -7, 8]], dtype=np.int8)
+    pkg_w = np.array([[2, 3, 4, 5], [-1, -2, 1, 2], [7, 0, -3, 1]], dtype=np.int8)
+    # Linear KAT of tests/test_w8a8_contract.py:55-76 (with bias).
+    lin_x = torch.tensor([[1.0, -2.0, 3.0, -4.0]])
+    lin_w = torch.tensor([[2.0, 1.0, -1.0, 3.0], [-2.0, 4.0, 1.0, 0.0]])
+    lin_b = torch.tensor([0.5, -0.5])
+    lin_s = R.static_activation_scale(lin_x.abs().max())
+    lin_out, lin_acc = R.integer_linear_per_output_reference(lin_x, lin_w, activation_scale=lin_s, bias=lin_b)
+    np.savez_compressed(
+        HERE / "kat.npz",
+        quant_in=kat_in.numpy(), quant_out=kat_out.numpy(),
+        pkg_a=pkg_a, pkg_w=pkg_w,
+        pkg_acc=(torch.from_numpy(pkg_a).int() @ torch.from_numpy(pkg_w).int().T).numpy(),
+        lin_x=lin_x.numpy(), lin_w=lin_w.numpy(), lin_b=lin_b.numpy(), lin_s=lin_s.numpy(),
+        lin_out=lin_out.numpy(), lin_acc=lin_acc.numpy(),
+    )
+
+    # 2. Integer linear, small shapes, fp32 and fp16 inputs, per-token scale, +/- bias.
+    small = {}
+    for tag, (m, k, n, dtype) in {
+        "f32": (8, 512, 384, torch.float32),
+        "f16": (5, 768, 200, torch.float16),
+    }.items():
+        x, w = S.config1_inputs(seed=11, m=m, k=k, n=n)
+        x = x.to(dtype)
+        w = w.to(dtype)
+        g = torch.Generator().manual_seed(12)
+        bias = torch.randn(n, generator=g) * 0.1
+        scale = R.scale_from_absmax(x.float().abs().amax(-1, keepdim=True))
+        out, acc = R.integer_linear_per_output_reference(x, w, activation_scale=scale)
+        out_b, _ = R.integer_linear_per_output_reference(x, w, activation_scale=scale, bias=bias)
+        _, qw, ws = R.per_output_weight_qdq(w)
+        qa = R.quantize_symmetric(x, scale)
+        small.update({
+            f"{tag}_x": x.float().numpy() if dtype == torch.float32 else f16(x),
+            f"{tag}_w": w.float().numpy() if dtype == torch.float32 else f16(w),
+            f"{tag}_bias": bias.numpy(), f"{tag}_scale": scale.numpy(),
+            f"{tag}_out": out.numpy(), f"{tag}_out_bias": out_b.numpy(), f"{tag}_acc": acc.numpy(),
+            f"{tag}_qw": qw.numpy(), f"{tag}_ws": ws.numpy(), f"{tag}_qa": qa.numpy(),
+        })
+    np.savez_compressed(HERE / "linear_small.npz", **small)
+
+    # 3. Full config-1 linear (seed 0), stored as digests; inputs are rebuilt
+    #    from synthetic.config1_inputs at test time.
+    x, w = S.config1_inputs(seed=0)
+    scale = R.scale_from_absmax(x.abs().amax(-1, keepdim=True))
+    out, acc = R.integer_linear_per_output_reference(x, w, activation_scale=scale)
+    _, qw, ws = R.per_output_weight_qdq(w)
+    qa = R.quantize_symmetric(x, scale)
+    (HERE / "config1_digest.json").write_text(json.dumps({
+        "recipe": "synthetic.config1_inputs(seed=0) -> X fp32 [8,4096], W fp32 [12288,4096]",
+        "sha256_acc_int32": sha(acc.numpy()),
+        "sha256_qact_int8": sha(qa.numpy()),
+        "sha256_qweight_int8": sha(qw.numpy()),
+        "sha256_wscale_f32": sha(ws.numpy()),
+        "sha256_act_scale_f32": sha(scale.numpy()),
+        "sha256_out_f32": sha(out.numpy()),
+        "sha256_out_f16": sha(out.half().numpy()),
+        "acc_min": int(acc.min()), "acc_max": int(acc.max()),
+        "acc_row0_first8": acc[0, :8].tolist(),
+        "out_row0_first8": out[0, :8].tolist(),
+    }, indent=1) + "\n")
+
+    # 4. RMSNorm (eager reference) + per-token quant, with and without residual.
+    from nanopointllm.llama.lightweight_runner import LightweightRMSNorm
+    g = torch.Generator().manual_seed(21)
+    xs = torch.randn(8, 4096, generator=g).half()
+    rs = torch.randn(8, 4096, generator=g).half()
+    nw = (1.0 + 0.1 * torch.randn(4096, generator=g)).half()
+
+    class _Norm(torch.nn.Module):
+        def __init__(self, w):
+            super().__init__()
+            self.weight = torch.nn.Parameter(w, requires_grad=False)
+            self.variance_epsilon = 1e-6
+
+    norm = LightweightRMSNorm(_Norm(nw))
+    with torch.no_grad():
+        normed = norm(xs)
+        summed, normed_r = norm.residual_norm(xs, rs)
+    qn, sn = _quant(R, normed)
+    qr, sr = _quant(R, normed_r)
+    np.savez_compressed(
+        HERE / "rmsnorm_quant.npz", x=f16(xs), res=f16(rs), w=f16(nw), eps=np.float32(1e-6),
+        normed=f16(normed), q=qn, s=sn, summed=f16(summed), normed_res=f16(normed_r),
+        q_res=qr, s_res=sr,
+    )
+
+    # 5. SiLU * up in fp16 (HF act_fn), then per-token requant.
+    from transformers.activations import ACT2FN
+    g = torch.Generator().manual_seed(22)
+    gate = (torch.randn(8, 1024, generator=g) * 2.0).half()
+    up = torch.randn(8, 1024, generator=g).half()
+    with torch.no_grad():
+        h = ACT2FN["silu"](gate) * up
+    qh, sh = _quant(R, h)
+    np.savez_compressed(HERE / "silu_mul.npz", gate=f16(gate), up=f16(up), h=f16(h), q=qh, s=sh)
+
+    # 6. RoPE: HF LlamaRotaryEmbedding + apply_rotary_pos_emb on fp16.
+    from transformers import LlamaConfig
+    from transformers.models.llama.modeling_llama import LlamaRotaryEmbedding, apply_rotary_pos_emb
+    cfg = LlamaConfig(hidden_size=512, num_attention_heads=4, num_key_value_heads=4,
+                      head_dim=128, max_position_embeddings=4096, rope_theta=10000.0)
+    rot = LlamaRotaryEmbedding(cfg)
+    g = torch.Generator().manual_seed(23)
+    pos = torch.tensor([[0, 1, 7, 255, 256, 1023, 1087, 4000]])
+    qh16 = torch.randn(1, 4, pos.shape[1], 128, generator=g).half()
+    kh16 = torch.randn(1, 4, pos.shape[1], 128, generator=g).half()
+    with torch.no_grad():
+        cos, sin = rot(qh16, pos)
+        qr16, kr16 = apply_rotary_pos_emb(qh16, kh16, cos, sin)
+    np.savez_compressed(
+        HERE / "rope.npz", positions=pos[0].numpy(), cos=f16(cos[0]), sin=f16(sin[0]),
+        q=f16(qh16[0].transpose(0, 1)), k=f16(kh16[0].transpose(0, 1)),
+        q_rot=f16(qr16[0].transpose(0, 1)), k_rot=f16(kr16[0].transpose(0, 1)),
+    )
+
+    # 7. Paged decode attention (reference PyTorch path) + store_kvcache.
+    from nanopointllm.llama.paged_attention import _paged_decode_attention_pytorch, store_kvcache
+    g = torch.Generator().manual_seed(24)
+    B, H, Hkv, D, bs, nb = 4, 8, 4, 128, 16, 24
+    ctx = torch.tensor([37, 16, 1, 70], dtype=torch.int32)
+    bt = S.permuted_block_tables(B, 5, nb, seed=25)
+    kc = torch.zeros(nb, bs, Hkv, D)
+    vc = torch.zeros(nb, bs, Hkv, D)
+    for b in range(B):
+        n = int(ctx[b])
+        kt = torch.randn(n, Hkv, D, generator=g).half().float()
+        vt = torch.randn(n, Hkv, D, generator=g).half().float()
+        slots = torch.tensor([int(bt[b, p // bs]) * bs + p % bs for p in range(n)], dtype=torch.int32)
+        store_kvcache(kt, vt, kc, vc, slots)
+    q = torch.randn(B, H, D, generator=g).half().float()
+    att = _paged_decode_attention_pytorch(q, kc, vc, bt, ctx, D ** -0.5, H // Hkv)
+    np.savez_compressed(
+        HERE / "decode_attention.npz", q=f16(q), k_cache=f16(kc), v_cache=f16(vc),
+        block_tables=bt.numpy(), context_lens=ctx.numpy(), scale=np.float32(D ** -0.5),
+        groups=np.int32(H // Hkv), out=att.numpy(),
+    )
+
+    # 8. Tiny Llama, eager reference paged runner, every Linear replaced by the
+    #    integer golden (int8 x int8 -> int32, per-token dynamic activations).
+    #    Stock run (fp16 SDPA on CPU), then the same run with the SDPA the
+    #    reference calls evaluated in fp64 and rounded to fp16 (isolates the
+    #    W8A8 numerics from CPU fp16 attention rounding).
+    _tiny_model(R, S, "tiny_model.npz")
+    sdpa = torch.nn.functional.scaled_dot_product_attention
+
+    def sdpa_fp64(q, k, v, *args, **kwargs):
+        if kwargs.get("attn_mask") is not None:
+            kwargs["attn_mask"] = kwargs["attn_mask"].double()
+        return sdpa(q.double(), k.double(), v.double(), *args, **kwargs).to(q.dtype)
+
+    torch.nn.functional.scaled_dot_product_attention = sdpa_fp64
+    try:
+        _tiny_model(R, S, "tiny_model_fp64_attention.npz")
+    finally:
+        torch.nn.functional.scaled_dot_product_attention = sdpa
+    print("fixtures written to", HERE)
+
+
+def _quant(R, values: torch.Tensor):
+    s = R.scale_from_absmax(values.float().abs().amax(-1, keepdim=True))
+    return R.quantize_symmetric(values, s).numpy(), s.reshape(-1).numpy()
+
+
+def _tiny_model(R, S, fname: str) -> None:
+    from transformers import LlamaConfig, LlamaForCausalLM
+    from nanopointllm.engine.forward_context import ForwardContext, clear_forward_context, set_forward_context
+    from nanopointllm.engine.kv_pool import allocate_kv_pool
+    from nanopointllm.llama.inject_paged import inject_paged_attention
+    from nanopointllm.llama.lightweight_runner import build_lightweight_llama_runner
+
+    shape = S.TINY
+    cfg = LlamaConfig(
+        vocab_size=shape.vocab, hidden_size=shape.hidden, intermediate_size=shape.intermediate,
+        num_hidden_layers=shape.layers, num_attention_heads=shape.heads,
+        num_key_value_heads=shape.kv_heads, head_dim=shape.head_dim,
+        max_position_embeddings=shape.max_position, rope_theta=shape.rope_theta,
+        rms_norm_eps=shape.eps, tie_word_embeddings=False,
+    )
+    model = LlamaForCausalLM(cfg).eval()
+    sd = S.llama_weights(shape, seed=0)
+    missing, unexpected = model.load_state_dict({k: v.float() for k, v in sd.items()}, strict=False)
+    assert not unexpected and all("rotary" in k for k in missing), (missing, unexpected)
+    # fp16 parameters, fp32 rotary inv_freq buffer: the state a model loaded
+    # with from_pretrained(torch_dtype=float16) is in (model.half() would also
+    # round inv_freq to fp16).
+    for prm in model.parameters():
+        prm.data = prm.data.half()
+    assert model.model.rotary_emb.inv_freq.dtype == torch.float32
+
+    def int_linear_hook(module, inputs, output):
+        x = inputs[0]
+        flat = x.reshape(-1, x.shape[-1])
+        scale = R.scale_from_absmax(flat.float().abs().amax(-1, keepdim=True))
+        out, _ = R.integer_linear_per_output_reference(flat, module.weight, activation_scale=scale)
+        return out.to(x.dtype).reshape(*x.shape[:-1], module.weight.shape[0])
+
+    for mod in model.modules():
+        if isinstance(mod, torch.nn.Linear):
+            mod.register_forward_hook(int_linear_hook)
+
+    block_size, num_blocks = 16, 48
+    lengths = [37, 64, 20]
+    steps = 8
+    prompts = S.decode_prompts(len(lengths), shape.vocab, lengths, seed=2)
+    bt = S.permuted_block_tables(len(lengths), 6, num_blocks, seed=3)
+    pool = allocate_kv_pool(model, num_blocks, block_size, torch.device("cpu"), torch.float16)
+    inject_paged_attention(model, pool)
+    runner = build_lightweight_llama_runner(model, decode_graph_mode=False)
+
+    def slot(b, p):
+        return int(bt[b, p // block_size]) * block_size + p % block_size
+
+    tokens = [list(p) for p in prompts]
+    step_logits, step_tokens = [], []
+    with torch.inference_mode():
+        # prefill: all prompts flattened into one [1, T] pass
+        ids = torch.tensor([t for p in prompts for t in p]).unsqueeze(0)
+        pos = torch.cat([torch.arange(n) for n in lengths]).unsqueeze(0)
+        slots = torch.tensor([slot(b, p) for b, n in enumerate(lengths) for p in range(n)], dtype=torch.int32)
+        set_forward_context(ForwardContext(
+            slot_mapping=slots, block_tables=bt, context_lens=torch.tensor(lengths, dtype=torch.int32),
+            position_ids=pos, seq_lens=list(lengths)))
+        try:
+            logits = runner(input_ids=ids, position_ids=pos)
+        finally:
+            clear_forward_context()
+        last = torch.tensor(np.cumsum(lengths) - 1)
+        lg = logits[0, last].float()
+        step_logits.append(lg.numpy())
+        nxt = lg.argmax(-1).tolist()
+        step_tokens.append(nxt)
+        for b in range(len(lengths)):
+            tokens[b].append(nxt[b])
+        for _ in range(steps - 1):
+            ctx = [len(t) for t in tokens]
+            ids = torch.tensor([t[-1] for t in tokens]).unsqueeze(0)
+            pos = torch.tensor([n - 1 for n in ctx]).unsqueeze(0)
+            slots = torch.tensor([slot(b, n - 1) for b, n in enumerate(ctx)], dtype=torch.int32)
+            set_forward_context(ForwardContext(
+                slot_mapping=slots, block_tables=bt, context_lens=torch.tensor(ctx, dtype=torch.int32),
+                position_ids=pos, seq_lens=[1] * len(ctx)))
+            try:
+                logits = runner(input_ids=ids, position_ids=pos)
+            finally:
+                clear_forward_context()
+            lg = logits[0].float()
+            step_logits.append(lg.numpy())
+            nxt = lg.argmax(-1).tolist()
+            step_tokens.append(nxt)
+            for b in range(len(lengths)):
+                tokens[b].append(nxt[b])
+
+    np.savez_compressed(
+        HERE / fname,
+        shape=json.dumps(shape.as_dict()), weight_seed=np.int32(0), prompt_seed=np.int32(2),
+        lengths=np.array(lengths, np.int32), block_tables=bt.numpy(), block_size=np.int32(block_size),
+        num_blocks=np.int32(num_blocks), tokens=np.array(step_tokens, np.int32),
+        logits=np.stack(step_logits).astype(np.float32),
+    )
+
+
+if __name__ == "__main__":
+    main()

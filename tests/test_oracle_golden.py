@@ -1,0 +1,206 @@
+"""Pin the numpy oracle to the reference: its known-answer vectors and the
+fixtures made by running the reference (tests/golden/make_golden.py)."""
+from __future__ import annotations
+
+import hashlib
+import json
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import golden
+from oracle import model as OM
+from oracle import w8a8 as O
+
+
+def sha(a) -> str:
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+def test_rounding_clipping_kat():
+    kat = golden("kat.npz")
+    q = O.quantize_symmetric(kat["quant_in"], np.float32(1.0))
+    assert q.tolist() == [-127, -127, -2, -2, 2, 2, 127, 127]
+    np.testing.assert_array_equal(q, kat["quant_out"])
+
+
+def test_nonpositive_scale_fails_closed():
+    with pytest.raises(ValueError, match="positive"):
+        O.quantize_symmetric(np.ones(1, np.float32), np.float32(0.0))
+
+
+def test_int32_overflow_guard():
+    # w8a8.py:152-153: K * 127^2 must stay below 2^31.
+    k = (1 << 31) // (127 * 127) + 1
+    with pytest.raises(OverflowError):
+        O.int_matmul_nt(np.zeros((1, k), np.int8), np.zeros((1, k), np.int8))
+
+
+def test_package_integer_golden():
+    kat = golden("kat.npz")
+    np.testing.assert_array_equal(O.int_matmul_nt(kat["pkg_a"], kat["pkg_w"]), kat["pkg_acc"])
+
+
+def test_linear_kat_with_bias():
+    kat = golden("kat.npz")
+    out, acc = O.integer_linear_per_output_reference(
+        kat["lin_x"], kat["lin_w"], activation_scale=kat["lin_s"], bias=kat["lin_b"])
+    np.testing.assert_array_equal(acc, kat["lin_acc"])
+    np.testing.assert_array_equal(out, kat["lin_out"])
+
+
+@pytest.mark.parametrize("tag", ["f32", "f16"])
+def test_linear_small_bit_exact(tag):
+    g = golden("linear_small.npz")
+    x, w = g[f"{tag}_x"], g[f"{tag}_w"]
+    qa, sa = O.dynamic_per_token_quant(x)
+    np.testing.assert_array_equal(sa, g[f"{tag}_scale"])
+    np.testing.assert_array_equal(qa, g[f"{tag}_qa"])
+    qw, sw = O.per_output_weight_quant(w)
+    np.testing.assert_array_equal(qw, g[f"{tag}_qw"])
+    np.testing.assert_array_equal(sw, g[f"{tag}_ws"])
+    out, acc = O.integer_linear_per_output_reference(x, w, activation_scale=sa)
+    np.testing.assert_array_equal(acc, g[f"{tag}_acc"])
+    np.testing.assert_array_equal(out, g[f"{tag}_out"])
+    out_b, _ = O.integer_linear_per_output_reference(x, w, activation_scale=sa, bias=g[f"{tag}_bias"])
+    np.testing.assert_array_equal(out_b, g[f"{tag}_out_bias"])
+
+
+def test_config1_full_size_digest():
+    """Full config-1 linear (8x4096 @ 12288x4096, seed 0) against the
+    reference's digests: int8 activations, int8 weights, fp16 scales, int32
+    accumulators and the dequantised outputs, all bit-exact."""
+    from nanopointllm_b200 import synthetic as S
+    d = golden("config1_digest.json")
+    x, w = S.config1_inputs(seed=0)
+    x, w = x.numpy(), w.numpy()
+    qa, sa = O.dynamic_per_token_quant(x)
+    qw, sw = O.per_output_weight_quant(w)
+    acc = O.int_matmul_nt(qa, qw)
+    out = O.dequantize(acc, sa.reshape(-1), sw)
+    assert sha(sa) == d["sha256_act_scale_f32"]
+    assert sha(qa) == d["sha256_qact_int8"]
+    assert sha(qw) == d["sha256_qweight_int8"]
+    assert sha(sw) == d["sha256_wscale_f32"]
+    assert sha(acc) == d["sha256_acc_int32"]
+    assert sha(out) == d["sha256_out_f32"]
+    assert sha(out.astype(np.float16)) == d["sha256_out_f16"]
+
+
+def _int8_mismatch(a, b):
+    diff = np.abs(a.astype(np.int32) - b.astype(np.int32))
+    return int((diff > 0).sum()), int(diff.max())
+
+
+def test_rmsnorm_quant_against_reference():
+    """The reference's fp32 ``mean`` sums in a library-defined order; the oracle
+    sums in fp64. Bound: normed fp16 differs in <= 0.1% of elements by one fp16
+    ulp; int8 activations differ in <= 0.05% of elements by at most 1; scales
+    equal."""
+    g = golden("rmsnorm_quant.npz")
+    for res_key, normed_key, q_key, s_key in (
+        (None, "normed", "q", "s"), ("res", "normed_res", "q_res", "s_res")):
+        res = None if res_key is None else g[res_key]
+        q, s, normed, summed = O.rmsnorm_quant(g["x"], g["w"], float(g["eps"]), res)
+        if res is not None:
+            np.testing.assert_array_equal(summed, g["summed"])
+        ref = g[normed_key]
+        ndiff = normed.view(np.int16).astype(np.int32) - ref.view(np.int16).astype(np.int32)
+        assert np.abs(ndiff).max() <= 1
+        assert (ndiff != 0).mean() <= 1e-3
+        np.testing.assert_array_equal(s, g[s_key])
+        count, worst = _int8_mismatch(q, g[q_key])
+        assert worst <= 1 and count <= 0.0005 * q.size
+
+
+def test_quant_of_reference_normed_is_exact():
+    """Given the reference's own fp16 normed values the quantiser is bit-exact."""
+    g = golden("rmsnorm_quant.npz")
+    q, s = O.dynamic_per_token_quant(g["normed"])
+    np.testing.assert_array_equal(q, g["q"])
+    np.testing.assert_array_equal(s.reshape(-1), g["s"])
+
+
+def test_silu_mul_against_reference():
+    """fp64 SiLU rounded to fp16 vs the reference's fp32 SiLU: <= 0.1% of
+    elements differ, by one fp16 ulp; requant exact given the reference h."""
+    g = golden("silu_mul.npz")
+    h = O.silu_mul(g["gate"], g["up"])
+    d = h.view(np.int16).astype(np.int32) - g["h"].view(np.int16).astype(np.int32)
+    assert np.abs(d).max() <= 1 and (d != 0).mean() <= 1e-3
+    q, s = O.dynamic_per_token_quant(g["h"])
+    np.testing.assert_array_equal(q, g["q"])
+    np.testing.assert_array_equal(s.reshape(-1), g["s"])
+
+
+def test_rope_bit_exact_given_tables():
+    g = golden("rope.npz")
+    np.testing.assert_array_equal(O.apply_rope(g["q"], g["cos"], g["sin"]), g["q_rot"])
+    np.testing.assert_array_equal(O.apply_rope(g["k"], g["cos"], g["sin"]), g["k_rot"])
+
+
+def test_rope_tables_match_hf():
+    g = golden("rope.npz")
+    cos, sin = O.rope_tables(g["positions"], 128)
+    np.testing.assert_array_equal(cos, g["cos"])
+    np.testing.assert_array_equal(sin, g["sin"])
+
+
+def test_decode_attention_against_reference():
+    g = golden("decode_attention.npz")
+    out = O.paged_decode_attention(g["q"], g["k_cache"], g["v_cache"], g["block_tables"],
+                                   g["context_lens"], float(g["scale"]), int(g["groups"]))
+    np.testing.assert_allclose(out, g["out"], rtol=1e-5, atol=1e-5)
+
+
+def test_store_kvcache_reference_cases():
+    # tests/test_store_kvcache.py:45-79 patterns: scattered slots, padding skip.
+    k_cache = np.zeros((4, 4, 2, 8), np.float16)
+    v_cache = np.zeros_like(k_cache)
+    key = np.arange(4 * 2 * 8, dtype=np.float16).reshape(4, 2, 8)
+    O.store_kvcache(key, -key, k_cache, v_cache, np.array([-1, 5, -1, 12]))
+    np.testing.assert_array_equal(k_cache[1, 1], key[1])
+    np.testing.assert_array_equal(k_cache[3, 0], key[3])
+    np.testing.assert_array_equal(v_cache[3, 0], -key[3])
+    assert float(np.abs(k_cache).sum()) == float(np.abs(key[1]).sum() + np.abs(key[3]).sum())
+
+
+def _tiny_oracle_run(fixture):
+    from nanopointllm_b200 import synthetic as S
+    g = golden(fixture)
+    shape = S.LlamaShape(**json.loads(str(g["shape"])))
+    weights = {k: v.numpy() for k, v in S.llama_weights(shape, seed=int(g["weight_seed"])).items()}
+    prompts = S.decode_prompts(len(g["lengths"]), shape.vocab, g["lengths"].tolist(),
+                               seed=int(g["prompt_seed"]))
+    oracle = OM.W8A8LlamaOracle(weights, shape, int(g["num_blocks"]), int(g["block_size"]))
+    tokens, logits = OM.greedy_generate(oracle, prompts, g["block_tables"], steps=g["tokens"].shape[0])
+    return g, tokens, logits
+
+
+def test_tiny_model_bit_exact_vs_reference_with_exact_attention():
+    """Oracle model vs the reference eager paged runner (every Linear replaced
+    by the integer golden) whose SDPA is evaluated in fp64: identical greedy
+    tokens and bit-identical fp16 logits over prefill + 7 decode steps."""
+    g, tokens, logits = _tiny_oracle_run("tiny_model_fp64_attention.npz")
+    np.testing.assert_array_equal(tokens, g["tokens"])
+    np.testing.assert_array_equal(logits, g["logits"])
+
+
+def near_tie_step(logits: np.ndarray, tol: float) -> int:
+    """First step whose smallest top-2 logit margin over the batch is < tol."""
+    srt = np.sort(logits, axis=-1)
+    margins = (srt[..., -1] - srt[..., -2]).min(axis=1)
+    below = np.nonzero(margins < tol)[0]
+    return int(below[0]) if below.size else logits.shape[0]
+
+
+def test_tiny_model_vs_stock_reference_until_near_tie():
+    """Against the stock reference run (CPU fp16 SDPA): identical tokens and
+    logits within 5e-2 on every step before the first near-tie (top-2 margin
+    below 5e-3), where the reference's own fp16 attention rounding decides."""
+    g, tokens, logits = _tiny_oracle_run("tiny_model.npz")
+    stop = near_tie_step(g["logits"], 5e-3)
+    assert stop >= 3
+    np.testing.assert_array_equal(tokens[:stop], g["tokens"][:stop])
+    np.testing.assert_allclose(logits[:stop], g["logits"][:stop], atol=5e-2, rtol=0)
