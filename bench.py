@@ -1,0 +1,469 @@
+"""Benchmark: W8A8 decode tokens/s of a Llama-7B-architecture backbone at
+batch 8 and 1024-token context on B200, through libnpl_w8a8.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload: random-init 7B W8A8 (32 layers, hidden 4096, 32
+heads x 128, intermediate 11008, vocab 32003), batch 8, each sequence 513
+point-embedding rows ~N(0,1) + 511 text tokens (uniform ids) = 1024-token
+context prefilled through the same W8A8 runner, fp16 paged KV pool with
+block_size 256 and a randomly permuted block table, greedy decode. A step is
+one full decode step (32 layers + LM head + argmax) for the 8 sequences,
+replayed as one CUDA graph; ``value`` = 8 * N * K / max-over-ranks time.
+
+Every step streams 6.6 GB of int8 weights and ~4.3 GB of fp16 KV, both far
+larger than the 126 MB L2, so no L2 flush is inserted between steps.
+
+``e2e`` measures the same steps through the runner's public API the way a
+serving loop drives it: each step copies its metadata (token ids, positions,
+slots, context lengths, block tables) from pinned host memory to the device,
+replays the graph and reads the 8 greedy tokens back to the host.
+
+With --gpus N (torchrun, one process per GPU) every rank runs an independent
+replica on its own requests (data parallel, no collective in the step).
+
+``--impl reference`` times the reference's CPU W8A8 path on the host cores:
+the numpy port of the reference algorithm in oracle/ (the reference itself is
+Python/torch code that cannot run on the GPU box), on a bounded sample of the
+same workload (one decoder layer + the LM head per step, extrapolated to 32
+layers).
+"""
+from __future__ import annotations
+
+import argparse
+import importlib.util
+import json
+import os
+import pathlib
+import statistics
+import subprocess
+import sys
+import time
+
+REPO = pathlib.Path(__file__).resolve().parent
+METRIC = "W8A8 decode tokens/s (7B, bs=8, ctx 1024); int8-linear % of HBM roofline"
+BATCH = 8
+CTX = 1024
+POINT_TOKENS = 513
+BLOCK_SIZE = 256
+
+
+def _register_package() -> None:
+    if "nanopointllm_b200" in sys.modules:
+        return
+    pkg = REPO / "nano-pointllm_b200"
+    spec = importlib.util.spec_from_file_location(
+        "nanopointllm_b200", pkg / "__init__.py", submodule_search_locations=[str(pkg)])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules["nanopointllm_b200"] = mod
+    spec.loader.exec_module(mod)
+
+
+def _peaks() -> tuple[float, str]:
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+# ----------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi samples during the timed region (clocks + throttle reasons)."""
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=10)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax.append(float(f[2]))
+            except ValueError:
+                continue
+            for name, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------- our arm
+def build_runner(torch, shape, steps_total: int, device, seed: int):
+    from nanopointllm_b200 import runner as R
+    from nanopointllm_b200 import synthetic as S
+    blocks_per_seq = (CTX + steps_total + BLOCK_SIZE - 1) // BLOCK_SIZE
+    num_blocks = BATCH * blocks_per_seq + 4
+    weights = S.LazyLlamaWeights(shape, seed=seed, device=str(device))
+    run = R.W8A8LlamaRunner(shape, weights, device=device, num_blocks=num_blocks, block_size=BLOCK_SIZE)
+    bt = S.permuted_block_tables(BATCH, blocks_per_seq, num_blocks, seed=seed + 3).to(device)
+    return run, bt
+
+
+def prefill(torch, run, bt, device, seed: int):
+    """1024-token contexts: 513 point embeddings ~N(0,1) + 511 text tokens."""
+    from nanopointllm_b200 import runner as R
+    shape = run.shape
+    g = torch.Generator(device=device).manual_seed(seed + 7)
+    points = torch.randn(BATCH, POINT_TOKENS, shape.hidden, generator=g, device=device).half()
+    text = torch.randint(0, shape.vocab, (BATCH, CTX - POINT_TOKENS), generator=g, device=device)
+    emb = torch.cat([points, torch.nn.functional.embedding(text, run.embed)], dim=1).reshape(-1, shape.hidden)
+    pos = torch.arange(CTX, device=device).repeat(BATCH)
+    blk = torch.arange(CTX, device=device) // BLOCK_SIZE
+    off = torch.arange(CTX, device=device) % BLOCK_SIZE
+    slots = (bt[:, blk].long() * BLOCK_SIZE + off).reshape(-1).to(torch.int32)
+    R.set_forward_context(R.ForwardContext(
+        slot_mapping=slots, block_tables=bt, context_lens=torch.full((BATCH,), CTX, dtype=torch.int32, device=device),
+        position_ids=pos, seq_lens=[CTX] * BATCH))
+    try:
+        logits = run.forward(inputs_embeds=emb, position_ids=pos, last_only=True)
+    finally:
+        R.clear_forward_context()
+    return logits[0].argmax(-1)
+
+
+def step_metadata(torch, bt, step: int, device):
+    """Metadata of decode step `step` (0-based): the new token sits at
+    position CTX + step."""
+    p = CTX + step
+    positions = torch.full((BATCH,), p, dtype=torch.int64, device=device)
+    slots = (bt[:, p // BLOCK_SIZE].long() * BLOCK_SIZE + p % BLOCK_SIZE).to(torch.int32)
+    ctx = torch.full((BATCH,), p + 1, dtype=torch.int32, device=device)
+    return positions, slots, ctx
+
+
+def linear_bytes(m: int, n: int, k: int, out_cols: int, residual: bool) -> int:
+    """Algorithmic bytes of one W8A8 linear launch: int8 weight + int8
+    activations + fp32 scales + fp16 output (+ fp16 residual read)."""
+    return n * k + m * k + 4 * m + 4 * n + 2 * m * out_cols + (2 * m * out_cols if residual else 0)
+
+
+def op_bytes(shape, name: str, ctx_len: int) -> int:
+    m, h, i_, v = BATCH, shape.hidden, shape.intermediate, shape.vocab
+    qkv_n = (shape.heads + 2 * shape.kv_heads) * shape.head_dim
+    if name == "linear.qkv":
+        return linear_bytes(m, qkv_n, h, qkv_n, False)
+    if name == "linear.o":
+        return linear_bytes(m, h, shape.heads * shape.head_dim, h, True)
+    if name == "linear.gate_up":
+        return linear_bytes(m, 2 * i_, h, i_, False)
+    if name == "linear.down":
+        return linear_bytes(m, h, i_, h, True)
+    if name == "linear.lm_head":
+        return linear_bytes(m, v, h, v, False)
+    if name == "attention":
+        # fp16 K and V of every context token of every head, q in, out
+        return m * ctx_len * shape.kv_heads * shape.head_dim * 2 * 2 + 2 * 2 * m * shape.heads * shape.head_dim
+    return 0
+
+
+def run_ours(args, torch, dist, rank: int, world: int, device) -> dict | None:
+    from nanopointllm_b200 import _lib, runner as R
+    from nanopointllm_b200 import synthetic as S
+    shape = S.LLAMA_7B if args.layers == 32 else S.LlamaShape(**{**S.LLAMA_7B.as_dict(), "layers": args.layers})
+    n_eager = 2
+    steps_total = args.warmup + args.steps * 2 + n_eager + 2
+    run, bt = build_runner(torch, shape, steps_total, device, seed=1000 * rank)
+    first = prefill(torch, run, bt, device, seed=1000 * rank)
+    torch.cuda.synchronize()
+
+    graph = R.DecodeGraph(run, BATCH, bt.shape[1])
+    step = 0
+    positions, slots, ctx = step_metadata(torch, bt, step, device)
+    graph.load(first, positions, slots, ctx, bt)
+    graph.capture()
+
+    # device-resident metadata of every step, prepared before timing
+    meta = [step_metadata(torch, bt, s, device) for s in range(steps_total)]
+
+    def device_step(s: int):
+        positions, slots, ctx = meta[s]
+        graph.positions.copy_(positions)
+        graph.slots.copy_(slots)
+        graph.context_lens.copy_(ctx)
+        tok = graph.replay()
+        graph.ids.copy_(tok)
+        return tok
+
+    for _ in range(args.warmup):
+        device_step(step)
+        step += 1
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    clocks = ClockSampler(torch.cuda.current_device() if "CUDA_VISIBLE_DEVICES" not in os.environ
+                          else int(os.environ["CUDA_VISIBLE_DEVICES"].split(",")[torch.cuda.current_device()]))
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        device_step(step)
+        step += 1
+    e1.record(stream)
+    torch.cuda.synchronize()
+    clock_info = clocks.stop()
+    dev_ms = e0.elapsed_time(e1)
+    if dist is not None:
+        t = torch.tensor([dev_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dev_ms = float(t.item())
+        dist.barrier()
+
+    # ---- e2e: host metadata in (pinned), graph replay, tokens out to host
+    pin = lambda x: x.cpu().pin_memory()
+    host_meta = [tuple(pin(x) for x in meta[step + i]) for i in range(args.steps)]
+    host_bt = pin(bt)
+    host_ids = pin(graph.ids)
+    host_out = torch.empty(BATCH, dtype=torch.int64).pin_memory()
+    h2d = d2h = 0
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    e2 = torch.cuda.Event(enable_timing=True)
+    e3 = torch.cuda.Event(enable_timing=True)
+    e2.record(stream)
+    for i in range(args.steps):
+        positions, slots, ctx = host_meta[i]
+        graph.load(host_ids, positions, slots, ctx, host_bt, non_blocking=True)
+        tok = graph.replay()
+        host_out.copy_(tok, non_blocking=True)
+        stream.synchronize()
+        host_ids.copy_(host_out)
+        h2d = sum(x.numel() * x.element_size() for x in (host_ids, positions, slots, ctx, host_bt))
+        d2h = host_out.numel() * host_out.element_size()
+    e3.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e2.elapsed_time(e3)
+    step += args.steps
+    if dist is not None:
+        t = torch.tensor([e2e_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+
+    # ---- per-kernel device time (eager steps, CUDA events on the launch stream)
+    records: list[tuple[str, object, object]] = []
+
+    def timer(name, fn, *a, **kw):
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record(stream)
+        out = fn(*a, **kw)
+        s1.record(stream)
+        records.append((name, s0, s1))
+        return out
+
+    ctx_mid = CTX + step
+    run.timer = timer
+    for _ in range(n_eager):
+        positions, slots, ctx = meta[step]
+        R.set_forward_context(R.ForwardContext(slot_mapping=slots, block_tables=bt, context_lens=ctx,
+                                               position_ids=positions, seq_lens=[1] * BATCH))
+        try:
+            run.forward(graph.ids, position_ids=positions)
+        finally:
+            R.clear_forward_context()
+        step += 1
+    run.timer = None
+    torch.cuda.synchronize()
+    per_op: dict[str, list[float]] = {}
+    for name, s0, s1 in records:
+        per_op.setdefault(name, []).append(s0.elapsed_time(s1))
+    _lib.device_status()
+
+    if rank != 0:
+        return None
+    peak, peak_kind = _peaks()
+    lin_names = [n for n in per_op if n.startswith("linear.")]
+    lin_ms = sum(sum(per_op[n]) for n in lin_names)
+    lin_bytes = sum(op_bytes(shape, n, ctx_mid) * len(per_op[n]) for n in lin_names)
+    lin_launches = sum(len(per_op[n]) for n in lin_names)
+    achieved = lin_bytes / (lin_ms * 1e-3) / 1e9
+    kernels = {}
+    for name, times in per_op.items():
+        b = op_bytes(shape, name, ctx_mid)
+        avg = sum(times) / len(times)
+        kernels[name] = {"launches_per_step": len(times) // n_eager, "avg_us": round(avg * 1e3, 2),
+                         "share": None}
+        if b:
+            kernels[name]["gbs"] = round(b / (avg * 1e-3) / 1e9, 1)
+            kernels[name]["frac"] = round(b / (avg * 1e-3) / 1e9 / peak, 4)
+    tot = sum(sum(t) for t in per_op.values())
+    for name, times in per_op.items():
+        kernels[name]["share"] = round(sum(times) / tot, 4)
+
+    launches_per_step = shape.layers * 10 + 2
+    tokens = BATCH * world * args.steps
+    value = tokens / (dev_ms * 1e-3)
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(dev_ms / args.steps, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int8 (W8A8: int8 x int8 -> int32, fp16 activations/KV)",
+        "data": "synthetic (random-init 7B weights ~N(0,0.02); 513 point embeddings ~N(0,1) + 511 uniform text ids)",
+        "config": {"workload": "config3: W8A8 Llama-7B-arch decode step, batch 8, ctx 1024 (prefilled), "
+                               "block_size 256, permuted block table, greedy, CUDA graph",
+                   "batch_per_gpu": BATCH, "context": CTX, "layers": shape.layers,
+                   "parallelism": f"dp{world} (independent replicas)",
+                   "l2": "no flush: each step streams 6.6 GB int8 weights + ~4.3 GB fp16 KV (>> 126 MB L2)"},
+        "e2e": {"value": round(tokens / (e2e_ms * 1e-3), 2), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "gpu_launches": launches_per_step * args.steps,
+        "roofline": {"bound": "hbm", "kernel": "w8a8_linear_kernel (all 5 linears of the step)",
+                     "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": None,
+                     "algorithmic_bytes_per_step": lin_bytes // n_eager,
+                     "launches_per_step": lin_launches // n_eager},
+        "kernels": kernels,
+        "clocks": clock_info,
+    }
+    if not args.no_cpu_baseline and world == 1:
+        line["cpu_baseline"] = cpu_baseline(seconds=args.cpu_seconds)
+    return line
+
+
+# ------------------------------------------------------------- CPU arm
+def cpu_baseline(seconds: float = 20.0) -> dict:
+    """The oracle port of the reference CPU W8A8 decode math, timed on the
+    host cores on a bounded sample: one decoder layer (random int8 weights of
+    the 7B shapes, batch 8, 1024-token context) plus the final norm + LM head;
+    a step is extrapolated as 32 layers + head."""
+    import numpy as np
+    sys.path.insert(0, str(REPO))
+    from oracle import w8a8 as O
+    rng = np.random.default_rng(0)
+    h, inter, heads, d, v = 4096, 11008, 32, 128, 32003
+    q8 = lambda n, k: rng.integers(-127, 128, size=(n, k), dtype=np.int8)
+    sc = lambda n: O.scale_from_absmax(rng.random(n).astype(np.float32) + 0.5)
+    w = {"qkv": (q8(3 * h, h), sc(3 * h)), "o": (q8(h, h), sc(h)), "gate": (q8(inter, h), sc(inter)),
+         "up": (q8(inter, h), sc(inter)), "down": (q8(h, inter), sc(h))}
+    head = (q8(v, h), sc(v))
+    norm_w = np.ones(h, np.float16)
+    x = rng.standard_normal((BATCH, h)).astype(np.float16)
+    kc = rng.standard_normal((BATCH * 4, BLOCK_SIZE, heads, d)).astype(np.float16)
+    vc = rng.standard_normal((BATCH * 4, BLOCK_SIZE, heads, d)).astype(np.float16)
+    bt = np.arange(BATCH * 4).reshape(BATCH, 4)
+    ctx = np.full(BATCH, CTX)
+
+    def lin(a16, name, wt=None):
+        qw, sw = wt if wt is not None else w[name]
+        qa, sa = O.dynamic_per_token_quant(a16)
+        return O.w8a8_linear(qa, sa, qw, sw)[0]
+
+    def layer(hs):
+        n = O.rmsnorm(hs, norm_w, 1e-6)
+        qkv = lin(n, "qkv")
+        q = qkv[:, :h].reshape(BATCH, heads, d)
+        a = O.paged_decode_attention(q, kc, vc, bt, ctx, d ** -0.5).astype(np.float16).reshape(BATCH, h)
+        hs = (hs.astype(np.float32) + lin(a, "o").astype(np.float32)).astype(np.float16)
+        n = O.rmsnorm(hs, norm_w, 1e-6)
+        act = O.silu_mul(lin(n, "gate"), lin(n, "up"))
+        return (hs.astype(np.float32) + lin(act, "down").astype(np.float32)).astype(np.float16)
+
+    layer_t, head_t = [], []
+    t_end = time.perf_counter() + seconds
+    while True:
+        t0 = time.perf_counter()
+        y = layer(x)
+        t1 = time.perf_counter()
+        lin(O.rmsnorm(y, norm_w, 1e-6), None, head)
+        t2 = time.perf_counter()
+        layer_t.append(t1 - t0)
+        head_t.append(t2 - t1)
+        if time.perf_counter() > t_end or len(layer_t) >= 20:
+            break
+    step_s = 32 * statistics.median(layer_t) + statistics.median(head_t)
+    return {"value": round(BATCH / step_s, 4), "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"{len(layer_t)} x (1 of 32 decoder layers + final norm/LM head), batch 8, ctx 1024; "
+                      f"step = 32 x median layer ({statistics.median(layer_t):.3f} s) + head "
+                      f"({statistics.median(head_t):.3f} s); numpy, float64 BLAS for the exact int32 "
+                      f"dot products, all host threads",
+            "s_per_step": round(step_s, 3)}
+
+
+def run_reference(args, rank: int) -> dict | None:
+    if rank != 0:
+        return None
+    vals = []
+    for _ in range(args.warmup):
+        cpu_baseline(seconds=0.0)
+    for _ in range(args.steps):
+        vals.append(cpu_baseline(seconds=0.0))
+    v = statistics.median(x["value"] for x in vals)
+    cb = dict(vals[0])
+    cb["value"] = v
+    cb["sample"] = f"per step: {cb['sample']}"
+    return {"metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(1e3 * BATCH / v, 1), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "impl": "reference", "dtype": "int8 (W8A8) on CPU",
+            "data": "synthetic", "config": {"workload": "config3 decode step (bounded CPU sample)"},
+            "cpu_baseline": cb, "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                                        "d2h_bytes_per_step": 0}}
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--layers", type=int, default=32, help="fewer layers only for quick checks (not the metric)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=20.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if args.impl == "reference":
+        line = run_reference(args, rank)
+        if line:
+            print(json.dumps(line))
+        return 0
+
+    import torch
+    _register_package()
+    dist = None
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
+    try:
+        line = run_ours(args, torch, dist, rank, world, device)
+    finally:
+        if dist is not None:
+            dist.destroy_process_group()
+    if line:
+        print(json.dumps(line))
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,152 @@
+/*
+ * libnpl_w8a8 — C ABI of the B200 (sm_100a) W8A8 linear + paged-decode path.
+ *
+ * Every entry takes device pointers, sizes and strides (in elements unless a
+ * name says bytes) and a CUDA stream passed as `void*` (a cudaStream_t; NULL
+ * is the legacy default stream). Work is enqueued on that stream; no entry
+ * synchronises the host, allocates or frees device memory, so every call can
+ * be recorded into a CUDA graph. Buffers, including workspaces, belong to the
+ * caller.
+ *
+ * Return value: NPL_OK or an NPL_ERR_* code; npl_last_error_string() gives
+ * the message (per host thread). Arguments are validated on the host before
+ * any launch. Device-side waits are bounded (~1 s); a kernel that gives up
+ * records a code in the per-device status word read by npl_device_status().
+ *
+ * Reference interfaces replaced (paths in the nanopointllm project):
+ *   nanopointllm/compression/w8a8.py        the W8A8 numeric contract
+ *   nanopointllm/llama/lightweight_runner.py RMSNorm / MLP / LM-head call sites
+ *   nanopointllm/llama/paged_attention.py    QKV / O call sites, rotary_fn +
+ *                                            store_kvcache, paged_decode_attention
+ */
+#ifndef NPL_W8A8_H_
+#define NPL_W8A8_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define NPL_OK 0
+#define NPL_ERR_ARG 1         /* null pointer, bad shape, stride or alignment   */
+#define NPL_ERR_OVERFLOW 2    /* K * 127^2 >= 2^31 (w8a8.py:152-153)             */
+#define NPL_ERR_LAUNCH 3      /* CUDA launch / driver error                      */
+#define NPL_ERR_TIMEOUT 4     /* a bounded device wait expired                   */
+#define NPL_ERR_UNSUPPORTED 5 /* not an sm_100 device, or a shape outside scope  */
+
+/* element types */
+#define NPL_F32 0
+#define NPL_F16 1
+
+/* fused epilogues of npl_w8a8_linear */
+#define NPL_EPI_NONE 0     /* out = dequant(acc)                                  */
+#define NPL_EPI_RESIDUAL 1 /* out = fp16(fp16(dequant(acc)) + residual)           */
+#define NPL_EPI_SILU_MUL 2 /* gate/up rows tile-interleaved; out = silu(g) * u    */
+
+const char* npl_last_error_string(void);
+int npl_version(void);
+
+/* Reads the per-device status word of the current device (synchronous; call
+ * it outside stream capture). *code receives 0 or the NPL_DEV_* code of the
+ * first expired wait; reset != 0 clears the word. Returns NPL_ERR_TIMEOUT
+ * when a code was set. */
+int npl_device_status(int* code, int reset);
+
+/*
+ * Per-row dynamic symmetric int8 quantisation (rows x cols, row stride ldx):
+ *   scale[r] = fp32(fp16(max(absmax_r, fp16.tiny) / 127)) (>= fp16.tiny)
+ *   q[r, c]  = clamp(rint(x / scale[r]), -127, 127)
+ * Replaces w8a8.py:33-43 quantize_symmetric + :46-50 scale_from_absmax, as
+ * used per token by :106-115 dynamic_per_token_activation_qdq and per output
+ * channel by :53-62 per_output_weight_qdq. x_dtype is NPL_F32 or NPL_F16.
+ * cols, ldx, ldq multiples of 16; pointers 16-byte aligned.
+ */
+int npl_quant_rows(const void* x, int x_dtype, int rows, int cols, int ldx, int8_t* q, int ldq,
+                   float* scale, void* stream);
+
+/*
+ * Fused RMSNorm + per-token int8 quantisation of fp16 rows (contiguous):
+ *   s = residual ? fp16(x + residual) : x            (sum_out <- s if given)
+ *   n = fp16(w * fp16(s * 1/sqrt(mean(s^2) + eps)))  (normed_out <- n if given)
+ *   q, scale = per-row quantisation of n             (as npl_quant_rows)
+ * Replaces lightweight_runner.py:239-260 (LightweightRMSNorm.forward /
+ * residual_norm, eager semantics) followed by w8a8.py:106-115. mean(s^2) is
+ * the fp64 sum of the squares divided by cols, rounded once to fp32.
+ */
+int npl_rmsnorm_quant(const void* x, const void* residual_or_null, const void* weight, float eps,
+                      int rows, int cols, void* sum_out_or_null, void* normed_out_or_null, int8_t* q,
+                      float* scale, void* stream);
+
+/*
+ * W8A8 linear: acc[m, n] = sum_k qa[m, k] * qw[n, k] (int32, exact), then
+ *   v = ((float)acc * sa[m]) * sw[n] (+ bias[n]), each step an fp32 rounding,
+ * and the epilogue:
+ *   NPL_EPI_NONE      out[m, n] = v as out_dtype (NPL_F32 or NPL_F16)
+ *   NPL_EPI_RESIDUAL  out[m, n] = fp16(fp16(v) + residual[m, n])       (fp16)
+ *   NPL_EPI_SILU_MUL  rows of qw are packed per 128-row tile t as 64 gate
+ *                     rows [64t, 64t+64) then the matching 64 up rows; out is
+ *                     [M, N/2] fp16 with out[m, j] = fp16(silu(g) * u),
+ *                     g = fp16(v_gate), u = fp16(v_up), silu(g) = fp16 of
+ *                     g / (1 + exp(-g)) evaluated in fp64.
+ * acc_out_or_null receives the int32 accumulators [M, N] (row stride N).
+ * Replaces w8a8.py:118-139 integer_linear_per_output_reference and the
+ * projection call sites paged_attention.py:97-124,283-305,1349-1352,1488 and
+ * lightweight_runner.py:320-404,675-681 (F.linear on packed QKV, O, packed
+ * gate/up + act_fn(gate)*up, down, LM head).
+ * K multiple of 16 and K*127^2 < 2^31; lda, ldw multiples of 16; int8
+ * operands 16-byte aligned. The workspace (npl_linear_workspace_bytes) must be
+ * zero-filled once by the caller; every call leaves it zeroed again. Calls
+ * that share a workspace must be ordered on one stream.
+ */
+size_t npl_linear_workspace_bytes(int M, int N, int K);
+int npl_w8a8_linear(const int8_t* qa, int lda, const float* sa, const int8_t* qw, int ldw,
+                    const float* sw, const float* bias_or_null, int M, int N, int K, int epilogue,
+                    const void* residual_or_null, int ld_res, void* out, int ld_out, int out_dtype,
+                    int32_t* acc_out_or_null, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * store_kvcache (paged_attention.py:353-383): key/value fp16 [T, Hkv, D]
+ * (token stride ld_tok) are written to cache slot slot_mapping[t] (block =
+ * slot / block_size, offset = slot % block_size) of the caches
+ * [num_blocks, block_size, Hkv, D]; negative slots are skipped.
+ */
+int npl_store_kv(const void* key, const void* value, int ld_tok, int T, int Hkv, int D,
+                 const int32_t* slot_mapping, void* k_cache, void* v_cache, int num_blocks,
+                 int block_size, void* stream);
+
+/*
+ * RoPE + store on the packed QKV projection output (paged_attention.py:
+ * 1284-1294: rotary_fn(q, k, cos, sin) then store_kvcache): qkv fp16
+ * [T, (H + 2*Hkv) * D] (row stride ld_qkv) holds q | k | v. With cos/sin the
+ * fp16 tables [max_position, D] indexed by positions[t] (int64),
+ *   rot(x) = fp16(fp16(x * cos) + fp16(rotate_half(x) * sin))
+ * q_out [T, H, D] <- rot(q); rot(k) and v are stored as npl_store_kv does.
+ */
+int npl_rope_store_kv(const void* qkv, int ld_qkv, int T, int H, int Hkv, int D, const void* cos_table,
+                      const void* sin_table, int max_position, const int64_t* positions,
+                      const int32_t* slot_mapping, void* q_out, void* k_cache, void* v_cache,
+                      int num_blocks, int block_size, void* stream);
+
+/*
+ * Decode-only paged attention (q_len = 1), paged_attention.py:872-1030:
+ * q fp16 [B, H, D] contiguous; caches fp16 [num_blocks, block_size, Hkv, D];
+ * block_tables int32 [B, bt_stride] (first max_blocks entries used);
+ * context_lens int32 [B]. out fp16 [B, H, D]. Softmax in fp32 over the
+ * context; a row with context_len 0 (padded bucket row) yields zeros. The
+ * workspace (npl_decode_attention_workspace_bytes) must be zero-filled once;
+ * calls leave it zeroed.
+ */
+size_t npl_decode_attention_workspace_bytes(int B, int H, int D, int max_blocks, int block_size);
+int npl_paged_decode_attention(const void* q, int B, int H, int Hkv, int D, const void* k_cache,
+                               const void* v_cache, int num_blocks, int block_size,
+                               const int32_t* block_tables, int bt_stride, int max_blocks,
+                               const int32_t* context_lens, float scale, void* out, void* workspace,
+                               size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NPL_W8A8_H_ */

@@ -1,0 +1,251 @@
+// Shared device/host helpers for libnpl_w8a8 (sm_100a only).
+//
+// Numerics rule for every kernel of the W8A8 contract: fp32 steps that must
+// match the reference bit for bit use the explicit round-to-nearest intrinsics
+// (__fmul_rn, __fadd_rn, __fdiv_rn, __fsqrt_rn), so the compiler cannot fuse
+// them into FMAs; the library is built without --use_fast_math.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/npl_w8a8.h"
+
+#if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ != 1000)
+#error "libnpl_w8a8 targets sm_100a only"
+#endif
+
+namespace npl {
+
+// ---------------------------------------------------------------- host side
+void set_error(const char* fmt, ...);
+int fail(int code, const char* fmt, ...);
+int launch_status(const char* what);   // maps cudaGetLastError to NPL_ERR_LAUNCH
+int num_sms();                         // cached per current device
+int* device_status_ptr();              // address of the per-device error word
+int check_device();                    // NPL_OK on an sm_100 device
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// ------------------------------------------------------------- device side
+// Error word shared by all kernels of the library on this device. A kernel
+// that gives up a bounded wait stores its NPL_DEV_* code here; the host reads
+// it with npl_device_status().
+enum DeviceError : int {
+  NPL_DEV_OK = 0,
+  NPL_DEV_TIMEOUT_TMA = 1,
+  NPL_DEV_TIMEOUT_MMA = 2,
+  NPL_DEV_TIMEOUT_EPILOGUE = 3,
+  NPL_DEV_TIMEOUT_TEARDOWN = 4,
+};
+
+constexpr float kFp16Tiny = 6.103515625e-05f;  // torch.finfo(torch.float16).tiny = 2^-14
+
+// scale_from_absmax (w8a8.py:46-50): fp32(fp16(max(absmax, tiny) / 127)), >= tiny.
+__device__ __forceinline__ float scale_from_absmax(float absmax) {
+  const float raw = __fdiv_rn(fmaxf(absmax, kFp16Tiny), 127.0f);
+  return fmaxf(__half2float(__float2half_rn(raw)), kFp16Tiny);
+}
+
+// quantize_symmetric (w8a8.py:33-43): clamp(rint(v / s), -127, 127).
+__device__ __forceinline__ int quantize_one(float v, float s) {
+  const int q = __float2int_rn(__fdiv_rn(v, s));
+  return max(-127, min(127, q));
+}
+
+template <typename T>
+__device__ __forceinline__ T warp_max(T v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+template <typename T>
+__device__ __forceinline__ T warp_sum(T v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Block-wide reductions for blockDim.x <= 1024 (multiple of 32); every thread
+// receives the result. `red` is shared scratch of >= 32 elements.
+template <typename T>
+__device__ __forceinline__ T block_max(T v, T* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  v = warp_max(v);
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  v = lane < nw ? red[lane] : red[0];
+  return warp_max(v);
+}
+
+template <typename T>
+__device__ __forceinline__ T block_sum(T v, T* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  v = warp_sum(v);
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  v = lane < nw ? red[lane] : T(0);
+  return warp_sum(v);
+}
+
+// Upper bound of any single wait in device code: ~1 s of wall time.
+constexpr uint64_t kWaitLimitNs = 1000000000ull;
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// Bounded wait on an mbarrier phase. Returns false (and records `code` in the
+// device error word) once ~kWaitLimitNs have passed without completion.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    for (int i = 0; i < 64; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      if (status) atomicExch(status, code);
+      return false;
+    }
+  }
+}
+
+// 2-D tiled TMA load into shared memory, completion counted on `bar`.
+// c0 is the innermost (contiguous) coordinate in elements, c1 the row.
+__device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, int c0, int c1,
+                                            uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ uint64_t policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+__device__ __forceinline__ uint64_t policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+__device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// ------------------------------------------------------------ tcgen05 / TMEM
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// MMA completion (of all previously issued tcgen05.mma of this thread) arrives
+// once on `bar`.
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T, int8 x int8 -> int32 (kind::i8).
+__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                       uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// 32 lanes x 8 consecutive 32-bit columns; thread i of the warp gets lane
+// (base lane + i), columns [col, col + 8).
+__device__ __forceinline__ void tmem_ld_x8(uint32_t taddr, int32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+                 "=r"(r[7])
+               : "r"(taddr));
+}
+
+// Instruction descriptor of kind::i8: signed int8 A and B, both K-major, int32
+// accumulator, M rows (A) x N columns (B). Bit layout: c_format [4,6) = 2
+// (S32), a_format [7,10) = 1 (INT8), b_format [10,13) = 1, a/b major bits 15/16
+// = 0 (K-major), N >> 3 at [17,23), M >> 4 at [24,29).
+__host__ __device__ constexpr uint32_t idesc_i8(int m, int n) {
+  return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+// Shared-memory matrix descriptor for a K-major tile stored with the 128-byte
+// swizzle (each row's 128 bytes in one 128 B line, 16 B chunks XOR (row % 8),
+// 8-row atoms of 1024 B back to back): start >> 4 at [0,14), leading byte
+// offset 16 B (encoded 1) at [16,30), stride byte offset 1024 B (encoded 64)
+// at [32,46), descriptor version 1 at [46,48), layout SWIZZLE_128B (2) at
+// [61,64). Advancing along K inside the 128 B row moves the start address.
+__device__ __forceinline__ uint64_t sdesc_k_sw128(uint32_t smem_addr) {
+  return (uint64_t)((smem_addr >> 4) & 0x3FFFu) | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
+}
+
+}  // namespace npl

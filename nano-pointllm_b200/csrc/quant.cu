@@ -1,0 +1,202 @@
+// Per-row dynamic int8 quantisation and fused RMSNorm + quantisation.
+//
+// npl_quant_rows     <- w8a8.py:33-50,106-115 (and :53-62 applied to weight rows)
+// npl_rmsnorm_quant  <- lightweight_runner.py:239-260 (eager RMSNorm / residual_norm)
+//                       followed by w8a8.py:106-115
+//
+// One CTA per row; rows are short (decode: M <= 64 rows of 4096 or 11008), so
+// both kernels are latency-bound single passes over L2-resident data.
+#include <algorithm>
+#include <initializer_list>
+
+#include "npl_common.cuh"
+
+namespace npl {
+namespace {
+
+constexpr int kQuantThreads = 256;
+
+template <typename T>
+struct Vec;  // 16-byte vector of T
+template <>
+struct Vec<float> {
+  static constexpr int N = 4;
+  __device__ static void load(const float* p, float (&v)[4]) {
+    const float4 x = *reinterpret_cast<const float4*>(p);
+    v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
+  }
+};
+template <>
+struct Vec<__half> {
+  static constexpr int N = 8;
+  __device__ static void load(const __half* p, float (&v)[8]) {
+    const uint4 x = *reinterpret_cast<const uint4*>(p);
+    const __half2* h = reinterpret_cast<const __half2*>(&x);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __half22float2(h[i]);
+      v[2 * i] = f.x;
+      v[2 * i + 1] = f.y;
+    }
+  }
+};
+
+template <int N>
+__device__ __forceinline__ void store_q(int8_t* dst, const int (&q)[N]);
+template <>
+__device__ __forceinline__ void store_q<4>(int8_t* dst, const int (&q)[4]) {
+  char4 c = make_char4((char)q[0], (char)q[1], (char)q[2], (char)q[3]);
+  *reinterpret_cast<char4*>(dst) = c;
+}
+template <>
+__device__ __forceinline__ void store_q<8>(int8_t* dst, const int (&q)[8]) {
+  uint2 u;
+  u.x = (uint32_t)(q[0] & 0xff) | ((uint32_t)(q[1] & 0xff) << 8) | ((uint32_t)(q[2] & 0xff) << 16) |
+        ((uint32_t)(q[3] & 0xff) << 24);
+  u.y = (uint32_t)(q[4] & 0xff) | ((uint32_t)(q[5] & 0xff) << 8) | ((uint32_t)(q[6] & 0xff) << 16) |
+        ((uint32_t)(q[7] & 0xff) << 24);
+  *reinterpret_cast<uint2*>(dst) = u;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kQuantThreads) quant_rows_kernel(const T* __restrict__ x, int cols, int ldx,
+                                                                   int8_t* __restrict__ q, int ldq,
+                                                                   float* __restrict__ scale) {
+  __shared__ float red[32];
+  constexpr int V = Vec<T>::N;
+  const T* row = x + (size_t)blockIdx.x * ldx;
+  float amax = 0.f;
+  for (int c = threadIdx.x * V; c < cols; c += kQuantThreads * V) {
+    float v[V];
+    Vec<T>::load(row + c, v);
+#pragma unroll
+    for (int i = 0; i < V; ++i) amax = fmaxf(amax, fabsf(v[i]));
+  }
+  amax = block_max(amax, red);
+  const float s = scale_from_absmax(amax);
+  if (threadIdx.x == 0) scale[blockIdx.x] = s;
+  int8_t* qrow = q + (size_t)blockIdx.x * ldq;
+  for (int c = threadIdx.x * V; c < cols; c += kQuantThreads * V) {
+    float v[V];
+    Vec<T>::load(row + c, v);
+    int qi[V];
+#pragma unroll
+    for (int i = 0; i < V; ++i) qi[i] = quantize_one(v[i], s);
+    store_q<V>(qrow + c, qi);
+  }
+}
+
+// RMSNorm of one fp16 row (optionally x + residual) + per-token quantisation.
+// The row is staged in shared memory as fp16.
+__global__ void __launch_bounds__(kQuantThreads)
+    rmsnorm_quant_kernel(const __half* __restrict__ x, const __half* __restrict__ res,
+                         const __half* __restrict__ w, float eps, int cols, __half* __restrict__ sum_out,
+                         __half* __restrict__ normed_out, int8_t* __restrict__ q, float* __restrict__ scale) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __half* srow = reinterpret_cast<__half*>(smem_raw);
+  __shared__ double dred[32];
+  __shared__ float fred[32];
+  const size_t base = (size_t)blockIdx.x * cols;
+
+  // 1. s = x (+ residual, fp16 add), sum of squares in fp64 (squares of fp16
+  //    values are exact in fp32 and fp64).
+  double ss = 0.0;
+  for (int c = threadIdx.x * 8; c < cols; c += kQuantThreads * 8) {
+    float v[8];
+    Vec<__half>::load(x + base + c, v);
+    if (res) {
+      float r[8];
+      Vec<__half>::load(res + base + c, r);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = __half2float(__float2half_rn(__fadd_rn(v[i], r[i])));
+    }
+    uint4 packed;
+    __half2* hp = reinterpret_cast<__half2*>(&packed);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) hp[i] = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+    *reinterpret_cast<uint4*>(srow + c) = packed;
+    if (res && sum_out) *reinterpret_cast<uint4*>(sum_out + base + c) = packed;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ss += (double)v[i] * (double)v[i];
+  }
+  ss = block_sum(ss, dred);
+  // mean rounded once to fp32; + eps; IEEE 1/sqrt (torch.rsqrt on CPU).
+  const float mean = __double2float_rn(ss / (double)cols);
+  const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+
+  // 2. n = fp16(w * fp16(s * r)); absmax of n.
+  float amax = 0.f;
+  for (int c = threadIdx.x * 8; c < cols; c += kQuantThreads * 8) {
+    float v[8], wv[8];
+    Vec<__half>::load(srow + c, v);
+    Vec<__half>::load(w + c, wv);
+    uint4 packed;
+    __half* hp = reinterpret_cast<__half*>(&packed);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float y = __half2float(__float2half_rn(__fmul_rn(v[i], r)));
+      hp[i] = __float2half_rn(__fmul_rn(wv[i], y));
+      amax = fmaxf(amax, fabsf(__half2float(hp[i])));
+    }
+    *reinterpret_cast<uint4*>(srow + c) = packed;
+    if (normed_out) *reinterpret_cast<uint4*>(normed_out + base + c) = packed;
+  }
+  amax = block_max(amax, fred);
+  const float s = scale_from_absmax(amax);
+  if (threadIdx.x == 0) scale[blockIdx.x] = s;
+
+  // 3. quantise (each thread re-reads only the chunks it wrote).
+  for (int c = threadIdx.x * 8; c < cols; c += kQuantThreads * 8) {
+    float v[8];
+    Vec<__half>::load(srow + c, v);
+    int qi[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) qi[i] = quantize_one(v[i], s);
+    store_q<8>(q + base + c, qi);
+  }
+}
+
+}  // namespace
+}  // namespace npl
+
+using namespace npl;
+
+extern "C" int npl_quant_rows(const void* x, int x_dtype, int rows, int cols, int ldx, int8_t* q, int ldq,
+                              float* scale, void* stream) {
+  if (int rc = check_device()) return rc;
+  if (!x || !q || !scale) return fail(NPL_ERR_ARG, "npl_quant_rows: null pointer");
+  if (rows < 0 || cols <= 0 || cols % 16 || ldx < cols || ldx % 16 || ldq < cols || ldq % 16)
+    return fail(NPL_ERR_ARG, "npl_quant_rows: bad shape rows=%d cols=%d ldx=%d ldq=%d", rows, cols, ldx, ldq);
+  if (!aligned16(x) || !aligned16(q)) return fail(NPL_ERR_ARG, "npl_quant_rows: pointers must be 16-byte aligned");
+  if (rows == 0) return NPL_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (x_dtype == NPL_F32)
+    quant_rows_kernel<float><<<rows, kQuantThreads, 0, st>>>(static_cast<const float*>(x), cols, ldx, q, ldq, scale);
+  else if (x_dtype == NPL_F16)
+    quant_rows_kernel<__half><<<rows, kQuantThreads, 0, st>>>(static_cast<const __half*>(x), cols, ldx, q, ldq, scale);
+  else
+    return fail(NPL_ERR_ARG, "npl_quant_rows: x_dtype must be NPL_F32 or NPL_F16");
+  return launch_status("npl_quant_rows");
+}
+
+extern "C" int npl_rmsnorm_quant(const void* x, const void* residual, const void* weight, float eps, int rows,
+                                 int cols, void* sum_out, void* normed_out, int8_t* q, float* scale,
+                                 void* stream) {
+  if (int rc = check_device()) return rc;
+  if (!x || !weight || !q || !scale) return fail(NPL_ERR_ARG, "npl_rmsnorm_quant: null pointer");
+  if (rows < 0 || cols <= 0 || cols % 16 || cols > 48 * 1024)
+    return fail(NPL_ERR_ARG, "npl_rmsnorm_quant: bad shape rows=%d cols=%d", rows, cols);
+  for (const void* p : std::initializer_list<const void*>{x, residual, weight, sum_out, normed_out, (const void*)q})
+    if (p && !aligned16(p)) return fail(NPL_ERR_ARG, "npl_rmsnorm_quant: pointers must be 16-byte aligned");
+  if (rows == 0) return NPL_OK;
+  const size_t smem = (size_t)cols * sizeof(__half);
+  if (smem > 48 * 1024) {
+    if (cudaFuncSetAttribute(rmsnorm_quant_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+        cudaSuccess)
+      return launch_status("npl_rmsnorm_quant: smem attribute");
+  }
+  rmsnorm_quant_kernel<<<rows, kQuantThreads, smem, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __half*>(x), static_cast<const __half*>(residual), static_cast<const __half*>(weight), eps,
+      cols, static_cast<__half*>(sum_out), static_cast<__half*>(normed_out), q, scale);
+  return launch_status("npl_rmsnorm_quant");
+}

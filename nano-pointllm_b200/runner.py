@@ -1,0 +1,292 @@
+"""W8A8 Llama runner over the paged KV pool: the drop-in for the reference's
+``LightweightLlamaRunner`` on the W8A8 path.
+
+Reference structure followed (nanopointllm):
+  engine/forward_context.py:10-39       ForwardContext (slot_mapping, block_tables,
+                                          context_lens, position_ids, seq_lens)
+  llama/lightweight_runner.py:625-736   LightweightLlamaRunner.forward
+  llama/lightweight_runner.py:480-560   LightweightLlamaLayer.forward (eager semantics:
+                                          RMSNorm, attention, fp16 residual, RMSNorm, MLP,
+                                          fp16 residual)
+  llama/paged_attention.py:1271-1488    PagedLlamaAttention.forward (QKV, rotary_fn,
+                                          store_kvcache, decode / prefill attention, o_proj)
+  engine/cuda_graph.py:30-77            strict decode CUDA-graph capture / replay
+  engine/paged_model_runner.py:332-383  decode step: metadata in, greedy token out
+
+Every Linear (packed QKV, O, packed gate/up, down, LM head) is W8A8: int8
+weights quantised once per output channel, int8 activations quantised per
+token, int32 accumulation on the tensor cores, dequant fused into the linear's
+epilogue together with the residual add (O, down) and SiLU(gate) * up. The
+decode step per layer is 10 kernels of libnpl_w8a8 and nothing else:
+
+  rmsnorm+quant -> QKV -> RoPE+store -> paged attention -> quant ->
+  O(+residual) -> rmsnorm+quant -> gate/up(+SiLU*up) -> quant -> down(+residual)
+
+Prefill attention over multi-token rows uses torch SDPA per sequence on the
+pool (the reference runs its own Triton varlen kernel there); the prefill
+linears are the same tcgen05 kernels at M = prefill tokens.
+"""
+from __future__ import annotations
+
+import threading
+from dataclasses import dataclass, field
+from typing import Optional
+
+import torch
+import torch.nn.functional as F
+
+from . import _lib as L
+from . import paged_attention as PA
+from . import w8a8 as W
+from .rope import rope_tables
+from .synthetic import LlamaShape
+
+
+# ------------------------------------------------------------------ context
+@dataclass
+class ForwardContext:
+    """Per-step metadata, as nanopointllm/engine/forward_context.py:10-24."""
+    slot_mapping: torch.Tensor                    # [T] int32, -1 = skip
+    block_tables: Optional[torch.Tensor]          # [B, max_blocks] int32
+    context_lens: Optional[torch.Tensor]          # [B] int32
+    position_ids: Optional[torch.Tensor] = None   # [1, T] int64
+    seq_lens: list[int] = field(default_factory=list)
+
+
+_ctx = threading.local()
+
+
+def set_forward_context(ctx: Optional[ForwardContext]) -> None:
+    _ctx.value = ctx
+
+
+def get_forward_context() -> Optional[ForwardContext]:
+    return getattr(_ctx, "value", None)
+
+
+def clear_forward_context() -> None:
+    _ctx.value = None
+
+
+# ------------------------------------------------------------ fused norm
+def rmsnorm_quant(x: torch.Tensor, weight: torch.Tensor, eps: float, residual: torch.Tensor | None = None, *,
+                  sum_out: torch.Tensor | None = None, normed_out: torch.Tensor | None = None):
+    """RMSNorm (of x + residual when given) fused with per-token int8
+    quantisation. Returns (q int8 [M, K], scale fp32 [M], sum_out)."""
+    m, k = x.shape
+    q = torch.empty((m, k), dtype=torch.int8, device=x.device)
+    s = torch.empty((m,), dtype=torch.float32, device=x.device)
+    if residual is not None and sum_out is None:
+        sum_out = torch.empty_like(x)
+    L.check(L.lib.npl_rmsnorm_quant(x.data_ptr(), L.ptr(residual), weight.data_ptr(), float(eps), m, k,
+                                    L.ptr(sum_out), L.ptr(normed_out), q.data_ptr(), s.data_ptr(),
+                                    L.stream_ptr(x.device)))
+    return q, s, sum_out
+
+
+class W8A8Layer:
+    def __init__(self, shape: LlamaShape, sd: dict[str, torch.Tensor], idx: int, device: torch.device,
+                 k_cache: torch.Tensor, v_cache: torch.Tensor):
+        p = f"model.layers.{idx}."
+
+        def w(name):
+            return sd[p + name].to(device=device, dtype=torch.float16)
+
+        qkv = torch.cat([w("self_attn.q_proj.weight"), w("self_attn.k_proj.weight"), w("self_attn.v_proj.weight")])
+        self.qkv = W.W8A8Linear.from_float(qkv)
+        self.o = W.W8A8Linear.from_float(w("self_attn.o_proj.weight"))
+        gq, gs = W.per_output_weight_quant(w("mlp.gate_proj.weight"))
+        uq, us = W.per_output_weight_quant(w("mlp.up_proj.weight"))
+        self.gate_up = W.W8A8Linear(W.pack_gate_up(gq, uq), W.pack_gate_up(gs, us))
+        self.down = W.W8A8Linear.from_float(w("mlp.down_proj.weight"))
+        self.input_norm = w("input_layernorm.weight").contiguous()
+        self.post_norm = w("post_attention_layernorm.weight").contiguous()
+        self.k_cache = k_cache
+        self.v_cache = v_cache
+
+
+class W8A8LlamaRunner:
+    """Replaces LightweightLlamaRunner for W8A8 serving on sm_100a.
+
+    ``forward(input_ids | inputs_embeds, position_ids)`` reads the paged
+    metadata from the thread-local ForwardContext and returns fp16 logits
+    [1, T, vocab] (or only each sequence's last row with ``last_only=True``).
+    """
+
+    def __init__(self, shape: LlamaShape, state_dict: dict[str, torch.Tensor], *, device: torch.device,
+                 kv_pool: torch.Tensor | None = None, num_blocks: int = 0, block_size: int = 256):
+        self.shape = shape
+        self.device = torch.device(device)
+        if kv_pool is None:
+            kv_pool = torch.zeros(2, shape.layers, num_blocks, block_size, shape.kv_heads, shape.head_dim,
+                                  dtype=torch.float16, device=self.device)
+        if kv_pool.dim() != 6 or kv_pool.dtype != torch.float16:
+            raise ValueError("kv_pool must be fp16 [2, layers, num_blocks, block_size, Hkv, D]")
+        self.kv_pool = kv_pool
+        self.block_size = kv_pool.shape[3]
+        self.num_blocks = kv_pool.shape[2]
+        self.embed = state_dict["model.embed_tokens.weight"].to(device=self.device, dtype=torch.float16)
+        self.layers = [W8A8Layer(shape, state_dict, i, self.device, kv_pool[0, i], kv_pool[1, i])
+                       for i in range(shape.layers)]
+        self.norm = state_dict["model.norm.weight"].to(device=self.device, dtype=torch.float16).contiguous()
+        self.lm_head = W.W8A8Linear.from_float(state_dict["lm_head.weight"].to(self.device, torch.float16))
+        self.cos, self.sin = rope_tables(shape.head_dim, shape.max_position, shape.rope_theta, self.device)
+        self.scale = shape.head_dim ** -0.5
+
+    @classmethod
+    def from_hf(cls, hf_model, kv_pool: torch.Tensor, device: torch.device | None = None) -> "W8A8LlamaRunner":
+        """Build from an HF LlamaForCausalLM (the engine's model) and the
+        engine's KV pool tensor (KVPool.pool, kv_pool.py:9-24)."""
+        cfg = hf_model.config
+        head_dim = getattr(cfg, "head_dim", None) or cfg.hidden_size // cfg.num_attention_heads
+        rope = getattr(cfg, "rope_parameters", None) or {}
+        shape = LlamaShape(hidden=cfg.hidden_size, heads=cfg.num_attention_heads,
+                           kv_heads=cfg.num_key_value_heads, head_dim=head_dim,
+                           intermediate=cfg.intermediate_size, layers=cfg.num_hidden_layers,
+                           vocab=cfg.vocab_size, rope_theta=float(rope.get("rope_theta", 10000.0)),
+                           eps=cfg.rms_norm_eps, max_position=cfg.max_position_embeddings)
+        device = device or kv_pool.device
+        return cls(shape, dict(hf_model.state_dict()), device=device, kv_pool=kv_pool)
+
+    # ------------------------------------------------------------- layers
+    def _attention(self, layer: W8A8Layer, q: torch.Tensor, ctx: ForwardContext) -> torch.Tensor:
+        """q [T, H, D] (rotated) -> [T, H*D] fp16."""
+        s = self.shape
+        t = q.shape[0]
+        if all(n == 1 for n in ctx.seq_lens):
+            out = PA.paged_decode_attention(q, layer.k_cache, layer.v_cache, ctx.block_tables, ctx.context_lens,
+                                            self.scale, s.heads // s.kv_heads)
+            return out.reshape(t, -1)
+        outs, off = [], 0
+        groups = s.heads // s.kv_heads
+        ctx_lens = ctx.context_lens.tolist()
+        for b, qlen in enumerate(ctx.seq_lens):
+            n = int(ctx_lens[b])
+            if qlen == 1:
+                o = PA.paged_decode_attention(q[off:off + 1], layer.k_cache, layer.v_cache,
+                                              ctx.block_tables[b:b + 1], ctx.context_lens[b:b + 1], self.scale, groups)
+                outs.append(o.reshape(1, -1))
+            else:
+                nblk = (n + self.block_size - 1) // self.block_size
+                bt = ctx.block_tables[b, :nblk].long()
+                k = layer.k_cache[bt].reshape(-1, s.kv_heads, s.head_dim)[:n]
+                v = layer.v_cache[bt].reshape(-1, s.kv_heads, s.head_dim)[:n]
+                qi = q[off:off + qlen].permute(1, 0, 2).unsqueeze(0)
+                ki = k.permute(1, 0, 2).unsqueeze(0).repeat_interleave(groups, 1)
+                vi = v.permute(1, 0, 2).unsqueeze(0).repeat_interleave(groups, 1)
+                prefix = n - qlen
+                if prefix == 0:
+                    o = F.scaled_dot_product_attention(qi, ki, vi, is_causal=True, scale=self.scale)
+                else:
+                    allowed = (torch.arange(n, device=q.device)[None, :]
+                               <= prefix + torch.arange(qlen, device=q.device)[:, None])
+                    o = F.scaled_dot_product_attention(qi, ki, vi, attn_mask=allowed, scale=self.scale)
+                outs.append(o[0].permute(1, 0, 2).reshape(qlen, -1))
+            off += qlen
+        return torch.cat(outs)
+
+    # Optional per-op timing hook: timer(name, fn, *args, **kwargs) -> fn(...)
+    # (used by bench.py to time each kernel with CUDA events on its stream).
+    timer = None
+
+    def _op(self, name: str, fn, *args, **kwargs):
+        if self.timer is None:
+            return fn(*args, **kwargs)
+        return self.timer(name, fn, *args, **kwargs)
+
+    def _layer(self, layer: W8A8Layer, h: torch.Tensor, positions: torch.Tensor, ctx: ForwardContext):
+        s, op = self.shape, self._op
+        xq, xs, _ = op("rmsnorm_quant", rmsnorm_quant, h, layer.input_norm, s.eps)
+        qkv = op("linear.qkv", W.linear_q, xq, xs, layer.qkv.qweight, layer.qkv.wscale)
+        q = op("rope_store", PA.rope_store_kvcache, qkv, s.heads, s.kv_heads, s.head_dim, self.cos, self.sin,
+               positions, ctx.slot_mapping, layer.k_cache, layer.v_cache)
+        attn = op("attention", self._attention, layer, q, ctx)
+        aq, asc = op("quant", W.dynamic_per_token_quant, attn)
+        h2 = op("linear.o", W.linear_q, aq, asc.reshape(-1), layer.o.qweight, layer.o.wscale,
+                epilogue=L.EPI_RESIDUAL, residual=h)
+        xq, xs, _ = op("rmsnorm_quant", rmsnorm_quant, h2, layer.post_norm, s.eps)
+        act = op("linear.gate_up", W.linear_q, xq, xs, layer.gate_up.qweight, layer.gate_up.wscale,
+                 epilogue=L.EPI_SILU_MUL)
+        aq, asc = op("quant", W.dynamic_per_token_quant, act)
+        return op("linear.down", W.linear_q, aq, asc.reshape(-1), layer.down.qweight, layer.down.wscale,
+                  epilogue=L.EPI_RESIDUAL, residual=h2)
+
+    @torch.inference_mode()
+    def forward(self, input_ids: torch.Tensor | None = None, *, inputs_embeds: torch.Tensor | None = None,
+                position_ids: torch.Tensor | None = None, last_only: bool = False) -> torch.Tensor:
+        ctx = get_forward_context()
+        if ctx is None:
+            raise RuntimeError("W8A8LlamaRunner.forward needs a ForwardContext (set_forward_context)")
+        if inputs_embeds is None:
+            if input_ids is None:
+                raise ValueError("input_ids or inputs_embeds is required")
+            h = F.embedding(input_ids.reshape(-1), self.embed)
+        else:
+            h = inputs_embeds.reshape(-1, self.shape.hidden).to(torch.float16).contiguous()
+        pos = position_ids if position_ids is not None else ctx.position_ids
+        pos = pos.reshape(-1).to(torch.int64).contiguous()
+        for layer in self.layers:
+            h = self._layer(layer, h, pos, ctx)
+        if last_only and not all(n == 1 for n in ctx.seq_lens):
+            last = torch.tensor([sum(ctx.seq_lens[:i + 1]) - 1 for i in range(len(ctx.seq_lens))],
+                                device=h.device)
+            h = h.index_select(0, last).contiguous()
+        xq, xs, _ = self._op("rmsnorm_quant", rmsnorm_quant, h, self.norm, self.shape.eps)
+        logits = self._op("linear.lm_head", W.linear_q, xq, xs, self.lm_head.qweight, self.lm_head.wscale)
+        return logits.unsqueeze(0)
+
+    __call__ = forward
+
+
+class DecodeGraph:
+    """Strict CUDA-graph decode step for a fixed batch and block-table width
+    (engine/cuda_graph.py:30-77): static metadata buffers, one replay per step,
+    greedy argmax inside the graph."""
+
+    def __init__(self, runner: W8A8LlamaRunner, batch: int, max_blocks: int):
+        dev = runner.device
+        self.runner = runner
+        self.ids = torch.zeros(batch, dtype=torch.int64, device=dev)
+        self.positions = torch.zeros(batch, dtype=torch.int64, device=dev)
+        self.slots = torch.full((batch,), -1, dtype=torch.int32, device=dev)
+        self.context_lens = torch.zeros(batch, dtype=torch.int32, device=dev)
+        self.block_tables = torch.zeros(batch, max_blocks, dtype=torch.int32, device=dev)
+        self.ctx = ForwardContext(slot_mapping=self.slots, block_tables=self.block_tables,
+                                  context_lens=self.context_lens, position_ids=self.positions,
+                                  seq_lens=[1] * batch)
+        self.graph: torch.cuda.CUDAGraph | None = None
+        self.logits: torch.Tensor | None = None
+        self.next_tokens: torch.Tensor | None = None
+
+    def _run(self):
+        set_forward_context(self.ctx)
+        try:
+            logits = self.runner.forward(self.ids, position_ids=self.positions)
+        finally:
+            clear_forward_context()
+        return logits, torch.argmax(logits[0], dim=-1)
+
+    def capture(self) -> None:
+        s = torch.cuda.Stream(device=self.runner.device)
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for _ in range(2):  # sizes every workspace before capture
+                self._run()
+        torch.cuda.current_stream().wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self.logits, self.next_tokens = self._run()
+        self.graph = g
+
+    def load(self, ids, positions, slots, context_lens, block_tables, non_blocking: bool = True) -> None:
+        self.ids.copy_(ids, non_blocking=non_blocking)
+        self.positions.copy_(positions, non_blocking=non_blocking)
+        self.slots.copy_(slots, non_blocking=non_blocking)
+        self.context_lens.copy_(context_lens, non_blocking=non_blocking)
+        self.block_tables.copy_(block_tables, non_blocking=non_blocking)
+
+    def replay(self) -> torch.Tensor:
+        if self.graph is None:
+            raise RuntimeError("capture() first")
+        self.graph.replay()
+        return self.next_tokens

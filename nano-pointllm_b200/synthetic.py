@@ -119,3 +119,30 @@ def permuted_block_tables(batch: int, blocks_per_seq: int, num_blocks: int, seed
     g = torch.Generator().manual_seed(seed)
     perm = torch.randperm(num_blocks, generator=g)[: batch * blocks_per_seq]
     return perm.reshape(batch, blocks_per_seq).to(torch.int32)
+
+
+class LazyLlamaWeights:
+    """Mapping name -> fp16 tensor generated on first access (on ``device``)
+    from a per-tensor seed, with the distributions of ``llama_weights``.
+
+    Lets a 7B-shaped random-init model be quantised tensor by tensor without
+    ever holding all fp16 weights at once."""
+
+    def __init__(self, shape: LlamaShape, seed: int = 0, device: str = "cuda"):
+        self.shape = shape
+        self.device = device
+        self._meta = {name: (i, shp, kind) for i, (name, shp, kind) in enumerate(llama_weight_names(shape))}
+        self.seed = seed
+
+    def __getitem__(self, name: str) -> torch.Tensor:
+        i, shp, kind = self._meta[name]
+        g = torch.Generator(device=self.device).manual_seed(self.seed * 1_000_003 + i)
+        t = torch.randn(shp, generator=g, device=self.device, dtype=torch.float32)
+        t = 1.0 + 0.1 * t if kind == "norm" else t * 0.02
+        return t.to(torch.float16)
+
+    def __contains__(self, name: str) -> bool:
+        return name in self._meta
+
+    def keys(self):
+        return self._meta.keys()

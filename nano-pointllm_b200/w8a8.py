@@ -1,0 +1,171 @@
+"""The W8A8 contract on the GPU, mirroring ``nanopointllm.compression.w8a8``.
+
+Same numerics as the reference (w8a8.py:14-139): symmetric int8 in
+[-127, 127], round-to-nearest-even, fp16-stored scales held as fp32,
+int8 x int8 -> int32 accumulation, dequant ((acc * s_a) * s_w) + bias in fp32.
+Every function runs the CUDA kernels of libnpl_w8a8 through its C ABI; inputs
+must be CUDA tensors (there is no CPU path).
+"""
+from __future__ import annotations
+
+from dataclasses import asdict, dataclass
+from typing import Any
+
+import torch
+
+from . import _lib as L
+
+
+@dataclass(frozen=True)
+class W8A8Contract:
+    """w8a8.py:14-30, unchanged."""
+    weight_bits: int = 8
+    activation_bits: int = 8
+    symmetric_min: int = -127
+    symmetric_max: int = 127
+    rounding: str = "round_to_nearest_ties_to_even"
+    scale_storage: str = "float16"
+    accumulator: str = "signed_int32"
+    bias: str = "floating_point_after_dequantization"
+    nonlinear_norm_residual: str = "bf16_or_fp16"
+
+    def as_dict(self) -> dict[str, Any]:
+        return asdict(self)
+
+
+CONTRACT = W8A8Contract()
+
+_DT = {torch.float32: L.NPL_F32, torch.float16: L.NPL_F16}
+
+
+def _require_cuda(*ts: torch.Tensor | None) -> None:
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ValueError("the W8A8 path runs on CUDA tensors only")
+
+
+def _rows(t: torch.Tensor) -> torch.Tensor:
+    t = t.reshape(-1, t.shape[-1])
+    return t if t.stride(-1) == 1 and t.stride(0) % 16 == 0 else t.contiguous()
+
+
+def dynamic_per_token_quant(values: torch.Tensor, *, out: torch.Tensor | None = None,
+                            scale_out: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """w8a8.py:106-115 (quantise step of dynamic_per_token_activation_qdq).
+
+    Returns (q int8 [..., K], scales fp32 [..., 1]).
+    """
+    _require_cuda(values)
+    if values.dtype not in _DT:
+        raise ValueError("values must be float16 or float32")
+    x = _rows(values)
+    rows, k = x.shape
+    q = out if out is not None else torch.empty((rows, k), dtype=torch.int8, device=x.device)
+    s = scale_out if scale_out is not None else torch.empty((rows,), dtype=torch.float32, device=x.device)
+    L.check(L.lib.npl_quant_rows(x.data_ptr(), _DT[x.dtype], rows, k, x.stride(0), q.data_ptr(), q.stride(0),
+                                 s.data_ptr(), L.stream_ptr(x.device)))
+    return q.reshape(values.shape), s.reshape(*values.shape[:-1], 1)
+
+
+def per_output_weight_quant(weight: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """w8a8.py:53-62 (per_output_weight_qdq): (qweight int8 [N, K], scales fp32 [N])."""
+    if weight.dim() < 2:
+        raise ValueError("weight must have at least two dimensions")
+    w = weight.detach().reshape(weight.shape[0], -1)
+    q, s = dynamic_per_token_quant(w)
+    return q.reshape(weight.shape), s.reshape(-1)
+
+
+def linear_workspace(device: torch.device, m: int, n: int, k: int) -> torch.Tensor:
+    nbytes = int(L.lib.npl_linear_workspace_bytes(m, n, k))
+    return L.workspaces.get(device, "linear", nbytes)
+
+
+def linear_q(qa: torch.Tensor, sa: torch.Tensor, qweight: torch.Tensor, wscale: torch.Tensor, *,
+             bias: torch.Tensor | None = None, epilogue: int = L.EPI_NONE,
+             residual: torch.Tensor | None = None, out: torch.Tensor | None = None,
+             out_dtype: torch.dtype = torch.float16, acc_out: torch.Tensor | None = None) -> torch.Tensor:
+    """int8 activations [M, K] (+ per-row fp32 scales) x int8 weight [N, K].
+
+    epilogue NONE -> [M, N] out_dtype; RESIDUAL -> fp16(fp16(v) + residual);
+    SILU_MUL (qweight rows tile-interleaved, see pack_gate_up) -> [M, N/2] fp16.
+    """
+    _require_cuda(qa, sa, qweight, wscale, bias, residual)
+    m, k = qa.shape
+    n = qweight.shape[0]
+    if qweight.shape[1] != k:
+        raise ValueError("linear input/weight shapes do not match")
+    cols = n // 2 if epilogue == L.EPI_SILU_MUL else n
+    if out is None:
+        out = torch.empty((m, cols), dtype=torch.float16 if epilogue else out_dtype, device=qa.device)
+    ws = linear_workspace(qa.device, m, n, k)
+    res = residual
+    L.check(L.lib.npl_w8a8_linear(
+        qa.data_ptr(), qa.stride(0), sa.data_ptr(), qweight.data_ptr(), qweight.stride(0), wscale.data_ptr(),
+        L.ptr(bias), m, n, k, epilogue, L.ptr(res), 0 if res is None else res.stride(0), out.data_ptr(),
+        out.stride(0), _DT[out.dtype], L.ptr(acc_out), ws.data_ptr(), ws.numel(), L.stream_ptr(qa.device)))
+    return out
+
+
+def integer_linear_per_output(values: torch.Tensor, weight: torch.Tensor, *,
+                              bias: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """GPU counterpart of w8a8.py:118-139 with dynamic per-token activation
+    scales (the dynamic_per_token mode): returns (out fp32, acc int32)."""
+    _require_cuda(values, weight)
+    if values.shape[-1] != weight.shape[1] or weight.dim() != 2:
+        raise ValueError("linear input/weight shapes do not match")
+    qa, sa = dynamic_per_token_quant(values)
+    qw, sw = per_output_weight_quant(weight)
+    qa2 = qa.reshape(-1, qa.shape[-1])
+    acc = torch.empty((qa2.shape[0], weight.shape[0]), dtype=torch.int32, device=values.device)
+    b = None if bias is None else bias.detach().float().contiguous()
+    out = linear_q(qa2, sa.reshape(-1), qw, sw, bias=b, out_dtype=torch.float32, acc_out=acc)
+    lead = values.shape[:-1]
+    return out.reshape(*lead, weight.shape[0]), acc.reshape(*lead, weight.shape[0])
+
+
+def pack_gate_up(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    """Row layout the SiLU*up epilogue reads: per 128-row tile t, gate rows
+    [64t, 64t+64) followed by up rows [64t, 64t+64). Works on weights [I, K]
+    or per-row scales [I]; I must be a multiple of 64."""
+    inter = gate.shape[0]
+    if inter % 64 or up.shape != gate.shape:
+        raise ValueError("gate/up must match and have a multiple of 64 rows")
+    g = gate.reshape(inter // 64, 64, *gate.shape[1:])
+    u = up.reshape(inter // 64, 64, *up.shape[1:])
+    return torch.stack([g, u], dim=1).reshape(2 * inter, *gate.shape[1:]).contiguous()
+
+
+class W8A8Linear:
+    """A quantised Linear: int8 weight [N, K] (row-major, K contiguous) with
+    per-output-channel fp32 scales (fp16 values) and an optional fp32 bias.
+
+    The drop-in for the reference's ``nn.Linear`` under W8A8 (weights from
+    per_output_weight_qdq, activations from dynamic per-token quantisation).
+    """
+
+    def __init__(self, qweight: torch.Tensor, wscale: torch.Tensor, bias: torch.Tensor | None = None):
+        if qweight.dtype != torch.int8 or qweight.dim() != 2:
+            raise ValueError("qweight must be int8 [N, K]")
+        self.qweight = qweight.contiguous()
+        self.wscale = wscale.float().contiguous()
+        self.bias = None if bias is None else bias.float().contiguous()
+
+    @classmethod
+    def from_float(cls, weight: torch.Tensor, bias: torch.Tensor | None = None) -> "W8A8Linear":
+        q, s = per_output_weight_quant(weight)
+        return cls(q, s, bias)
+
+    @property
+    def out_features(self) -> int:
+        return self.qweight.shape[0]
+
+    @property
+    def in_features(self) -> int:
+        return self.qweight.shape[1]
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        qa, sa = dynamic_per_token_quant(x)
+        out = linear_q(qa.reshape(-1, x.shape[-1]), sa.reshape(-1), self.qweight, self.wscale, bias=self.bias,
+                       out_dtype=torch.float16 if x.dtype == torch.float16 else torch.float32)
+        return out.reshape(*x.shape[:-1], self.out_features)

@@ -1,0 +1,49 @@
+"""CPU checks of the C ABI boundary: the library loads and exports exactly the
+entry points include/npl_w8a8.h declares (no compute call without a GPU)."""
+from __future__ import annotations
+
+import ctypes
+import re
+
+from conftest import REPO
+
+
+def declared_symbols() -> set[str]:
+    text = (REPO / "include" / "npl_w8a8.h").read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return set(re.findall(r"\b(npl_[a-z0-9_]+)\s*\(", text))
+
+
+def test_header_declares_the_path():
+    syms = declared_symbols()
+    for name in ("npl_quant_rows", "npl_rmsnorm_quant", "npl_w8a8_linear", "npl_linear_workspace_bytes",
+                 "npl_store_kv", "npl_rope_store_kv", "npl_paged_decode_attention",
+                 "npl_decode_attention_workspace_bytes", "npl_last_error_string", "npl_device_status"):
+        assert name in syms
+
+
+def test_library_exports_every_declared_symbol():
+    from nanopointllm_b200 import _lib
+    lib = ctypes.CDLL(str(_lib.LIB_PATH))
+    missing = [s for s in sorted(declared_symbols()) if not hasattr(lib, s)]
+    assert not missing, missing
+
+
+def test_binding_covers_header():
+    from nanopointllm_b200 import _lib
+    assert declared_symbols() == set(_lib.SIGNATURES)
+
+
+def test_version_and_error_string_without_device():
+    from nanopointllm_b200 import _lib
+    assert _lib.lib.npl_version() >= 1
+    assert isinstance(_lib.lib.npl_last_error_string(), bytes)
+
+
+def test_workspace_sizes_are_host_only():
+    from nanopointllm_b200 import _lib
+    n = _lib.lib.npl_linear_workspace_bytes(8, 12288, 4096)
+    # (SMs - 1) partial-tile slots of 8 token columns x 128 rows x int32 + counters
+    assert n >= 8 * 128 * 4
+    a = _lib.lib.npl_decode_attention_workspace_bytes(8, 32, 128, 5, 256)
+    assert a >= 8 * 32 * 5 * (128 + 2) * 4
