@@ -171,9 +171,11 @@ class W8A8LlamaRunner:
                 bt = ctx.block_tables[b, :nblk].long()
                 k = layer.k_cache[bt].reshape(-1, s.kv_heads, s.head_dim)[:n]
                 v = layer.v_cache[bt].reshape(-1, s.kv_heads, s.head_dim)[:n]
-                qi = q[off:off + qlen].permute(1, 0, 2).unsqueeze(0)
-                ki = k.permute(1, 0, 2).unsqueeze(0).repeat_interleave(groups, 1)
-                vi = v.permute(1, 0, 2).unsqueeze(0).repeat_interleave(groups, 1)
+                # fp32 operands: the reference evaluates this attention with fp32
+                # accumulation and no fp16 rounding of the probabilities
+                qi = q[off:off + qlen].permute(1, 0, 2).unsqueeze(0).float()
+                ki = k.permute(1, 0, 2).unsqueeze(0).repeat_interleave(groups, 1).float()
+                vi = v.permute(1, 0, 2).unsqueeze(0).repeat_interleave(groups, 1).float()
                 prefix = n - qlen
                 if prefix == 0:
                     o = F.scaled_dot_product_attention(qi, ki, vi, is_causal=True, scale=self.scale)
@@ -181,7 +183,7 @@ class W8A8LlamaRunner:
                     allowed = (torch.arange(n, device=q.device)[None, :]
                                <= prefix + torch.arange(qlen, device=q.device)[:, None])
                     o = F.scaled_dot_product_attention(qi, ki, vi, attn_mask=allowed, scale=self.scale)
-                outs.append(o[0].permute(1, 0, 2).reshape(qlen, -1))
+                outs.append(o[0].permute(1, 0, 2).reshape(qlen, -1).half())
             off += qlen
         return torch.cat(outs)
 
