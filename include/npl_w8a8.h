@@ -4,9 +4,9 @@
  * Every entry takes device pointers, sizes and strides (in elements unless a
  * name says bytes) and a CUDA stream passed as `void*` (a cudaStream_t; NULL
  * is the legacy default stream). Work is enqueued on that stream; no entry
- * synchronises the host, allocates or frees device memory, so every call can
- * be recorded into a CUDA graph. Buffers, including workspaces, belong to the
- * caller.
+ * synchronises the host, allocates or frees device memory. Apart from
+ * npl_w8a8_linear_noalloc (see its own comment), every call can be recorded
+ * into a CUDA graph. Buffers, including workspaces, belong to the caller.
  *
  * Return value: NPL_OK or an NPL_ERR_* code; npl_last_error_string() gives
  * the message (per host thread). Arguments are validated on the host before
@@ -105,6 +105,26 @@ int npl_w8a8_linear(const int8_t* qa, int lda, const float* sa, const int8_t* qw
                     const float* sw, const float* bias_or_null, int M, int N, int K, int epilogue,
                     const void* residual_or_null, int ld_res, void* out, int ld_out, int out_dtype,
                     int32_t* acc_out_or_null, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * npl_w8a8_linear without a workspace argument, for callers that cannot
+ * allocate device memory: a plugin inside a host engine that owns all device
+ * memory and passes only input/output buffers, a binding from a language
+ * without a CUDA allocator, or a loop that must not call cudaMalloc (it can
+ * synchronise the device). This entry point has no counterpart in the
+ * reference; it computes exactly what npl_w8a8_linear computes.
+ * Its scratch is a fixed array inside the library (~5 MiB per device, held
+ * until the process exits): M <= 64 tokens on devices with at most 160 SMs;
+ * larger M is rejected with NPL_ERR_ARG. Every call shares that array: calls
+ * that overlap on the GPU (other streams, other host threads) race and give
+ * wrong results. Each call clears the part it uses on its stream first. The
+ * first call on a device looks up the array's address; make it before any
+ * stream capture.
+ */
+int npl_w8a8_linear_noalloc(const int8_t* qa, int lda, const float* sa, const int8_t* qw, int ldw,
+                            const float* sw, const float* bias_or_null, int M, int N, int K, int epilogue,
+                            const void* residual_or_null, int ld_res, void* out, int ld_out, int out_dtype,
+                            int32_t* acc_out_or_null, void* stream);
 
 /*
  * store_kvcache (paged_attention.py:353-383): key/value fp16 [T, Hkv, D]

@@ -42,6 +42,7 @@ SIGNATURES = {
     "npl_rmsnorm_quant": (_I, [_P, _P, _P, _F, _I, _I, _P, _P, _P, _P, _P]),
     "npl_linear_workspace_bytes": (_Z, [_I, _I, _I]),
     "npl_w8a8_linear": (_I, [_P, _I, _P, _P, _I, _P, _P, _I, _I, _I, _I, _P, _I, _P, _I, _I, _P, _P, _Z, _P]),
+    "npl_w8a8_linear_noalloc": (_I, [_P, _I, _P, _P, _I, _P, _P, _I, _I, _I, _I, _P, _I, _P, _I, _I, _P, _P]),
     "npl_store_kv": (_I, [_P, _P, _I, _I, _I, _I, _P, _P, _P, _I, _I, _P]),
     "npl_rope_store_kv": (_I, [_P, _I, _I, _I, _I, _I, _P, _P, _I, _P, _P, _P, _P, _P, _I, _I, _P]),
     "npl_decode_attention_workspace_bytes": (_Z, [_I, _I, _I, _I, _I]),

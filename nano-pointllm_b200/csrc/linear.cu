@@ -508,3 +508,86 @@ extern "C" int npl_w8a8_linear(const int8_t* qa, int lda, const float* sa, const
     default: return launch_linear<256, 4>(tw, tx, p, st);
   }
 }
+
+// ----------------------------------------------------------------------------
+// npl_w8a8_linear_noalloc: the same linear for callers that cannot allocate.
+//
+// npl_w8a8_linear needs a caller-provided workspace for the partial tiles of
+// its stream-K split. Some callers cannot provide one: a plugin running inside
+// a host engine that owns every byte of device memory and hands the plugin
+// only its input and output buffers, a binding from a language that has no
+// CUDA allocator, or a latency-critical loop that must not call cudaMalloc
+// (which may synchronise the device). For them this entry point takes its
+// scratch from a fixed array in the library's own device memory instead.
+//
+// The array below is sized for at most 64 tokens (M <= 64) on a device with
+// at most 160 SMs: 159 partial-tile slots of 64 x 128 int32 plus their
+// counters, about 5 MiB. It exists once per device that loads the library and
+// stays allocated until the process exits. Every call uses the same array, so
+// calls must not overlap on the GPU: two calls in flight at the same time (on
+// different streams, or in different host threads) race on it and give wrong
+// results. Each call zeroes the part it uses (on the caller's stream) before
+// the kernel runs, so a call never depends on what an earlier call left there.
+// The first call on each device looks up the array's device address with
+// cudaGetSymbolAddress (with that device current); make that first call
+// before starting any stream capture.
+// ----------------------------------------------------------------------------
+namespace npl {
+namespace {
+
+constexpr int kNoAllocMaxTokens = 64;
+constexpr int kNoAllocMaxSlots = 159;  // grid - 1 for devices with up to 160 SMs
+constexpr size_t kNoAllocAccBytes = (size_t)kNoAllocMaxSlots * kNoAllocMaxTokens * kTileN * sizeof(int32_t);
+constexpr size_t kNoAllocBytes = kNoAllocAccBytes + ((kNoAllocMaxSlots * sizeof(int32_t) + 255) & ~size_t(255));
+
+static __device__ __align__(256) unsigned char g_linear_scratch[kNoAllocBytes];
+
+constexpr int kNoAllocDevices = 64;
+void* g_scratch_ptr[kNoAllocDevices];
+
+// Device address of g_linear_scratch on the current device (looked up once).
+int scratch_address(void** out) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocDevices)
+    return fail(NPL_ERR_LAUNCH, "npl_w8a8_linear_noalloc: no usable current device");
+  if (!g_scratch_ptr[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_linear_scratch);
+    if (e != cudaSuccess || !p)
+      return fail(NPL_ERR_LAUNCH, "npl_w8a8_linear_noalloc: cudaGetSymbolAddress failed: %s",
+                  cudaGetErrorString(e));
+    g_scratch_ptr[dev] = p;
+  }
+  *out = g_scratch_ptr[dev];
+  return NPL_OK;
+}
+
+}  // namespace
+}  // namespace npl
+
+extern "C" int npl_w8a8_linear_noalloc(const int8_t* qa, int lda, const float* sa, const int8_t* qw, int ldw,
+                                       const float* sw, const float* bias, int M, int N, int K, int epilogue,
+                                       const void* residual, int ld_res, void* out, int ld_out, int out_dtype,
+                                       int32_t* acc_out, void* stream) {
+  if (int rc = check_device()) return rc;
+  if (M > npl::kNoAllocMaxTokens)
+    return fail(NPL_ERR_ARG, "npl_w8a8_linear_noalloc: M = %d tokens, the built-in scratch holds at most %d", M,
+                npl::kNoAllocMaxTokens);
+  if (M <= 0 || N <= 0 || K <= 0) {
+    // shape errors (and M == 0) are reported by npl_w8a8_linear itself
+    return npl_w8a8_linear(qa, lda, sa, qw, ldw, sw, bias, M, N, K, epilogue, residual, ld_res, out, ld_out,
+                           out_dtype, acc_out, nullptr, 0, stream);
+  }
+  const size_t need = ws_bytes(M);
+  if (need > npl::kNoAllocBytes)
+    return fail(NPL_ERR_UNSUPPORTED,
+                "npl_w8a8_linear_noalloc: this device needs %zu scratch bytes, the built-in array has %zu "
+                "(more than %d SMs)",
+                need, npl::kNoAllocBytes, npl::kNoAllocMaxSlots + 1);
+  void* scratch = nullptr;
+  if (int rc = npl::scratch_address(&scratch)) return rc;
+  if (cudaMemsetAsync(scratch, 0, need, static_cast<cudaStream_t>(stream)) != cudaSuccess)
+    return launch_status("npl_w8a8_linear_noalloc: clearing the scratch");
+  return npl_w8a8_linear(qa, lda, sa, qw, ldw, sw, bias, M, N, K, epilogue, residual, ld_res, out, ld_out,
+                         out_dtype, acc_out, scratch, need, stream);
+}
