@@ -36,7 +36,6 @@ import json
 import os
 import pathlib
 import statistics
-import subprocess
 import sys
 import time
 
@@ -68,48 +67,51 @@ def _peaks() -> tuple[float, str]:
 
 # ----------------------------------------------------------------- clocks
 class ClockSampler:
-    """nvidia-smi samples during the timed region (clocks + throttle reasons)."""
-    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """SM clock and throttle reasons sampled every 10 ms through NVML while the
+    timed region runs (reading only; no setting is changed)."""
+    REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+               "sw_power_cap": 0x4}
 
     def __init__(self, gpu_index: int):
         self.idx = gpu_index
-        self.proc = None
+        self.samples: list[tuple[int, int, int]] = []
+        self._stop = None
+        self._thread = None
+        self.error = None
+
+    def _run(self):
+        import pynvml
+        try:
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.idx)
+            smax = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+            while not self._stop.is_set():
+                sm = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+                reasons = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                self.samples.append((sm, smax, reasons))
+                self._stop.wait(0.01)
+        except Exception as e:  # noqa: BLE001 - report, do not fail the bench
+            self.error = repr(e)
 
     def start(self):
-        try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except OSError:
-            self.proc = None
+        import threading
+        self._stop = threading.Event()
+        self._thread = threading.Thread(target=self._run, daemon=True)
+        self._thread.start()
 
     def stop(self) -> dict:
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        try:
-            out, _ = self.proc.communicate(timeout=10)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-            out, _ = self.proc.communicate()
-        sm, smax, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in out.strip().splitlines():
-            f = [x.strip() for x in line.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1]))
-                smax.append(float(f[2]))
-            except ValueError:
-                continue
-            for name, v in zip(names, f[5:9]):
-                if v.lower() == "active":
+        self._stop.set()
+        self._thread.join(timeout=5)
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [f"no samples: {self.error}"]}
+        reasons = set()
+        for _, _, r in self.samples:
+            for name, bit in self.REASONS.items():
+                if r & bit:
                     reasons.add(name)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        return {"sm_mhz": statistics.median(s[0] for s in self.samples),
+                "sm_max_mhz": max(s[1] for s in self.samples), "reasons": sorted(reasons),
+                "samples": len(self.samples)}
 
 
 # ------------------------------------------------------------- our arm
@@ -214,8 +216,9 @@ def run_ours(args, torch, dist, rank: int, world: int, device) -> dict | None:
         step += 1
     torch.cuda.synchronize()
     stream = torch.cuda.current_stream()
-    clocks = ClockSampler(torch.cuda.current_device() if "CUDA_VISIBLE_DEVICES" not in os.environ
-                          else int(os.environ["CUDA_VISIBLE_DEVICES"].split(",")[torch.cuda.current_device()]))
+    visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+    clocks = ClockSampler(int(visible.split(",")[torch.cuda.current_device()]) if visible
+                          else torch.cuda.current_device())
     if dist is not None:
         dist.barrier()
     torch.cuda.synchronize()
@@ -324,7 +327,7 @@ def run_ours(args, torch, dist, rank: int, world: int, device) -> dict | None:
     for name, times in per_op.items():
         kernels[name]["share"] = round(sum(times) / tot, 4)
 
-    launches_per_step = shape.layers * 10 + 2
+    launches_per_step = shape.layers * 9 + 2
     tokens = BATCH * world * args.steps
     value = tokens / (dev_ms * 1e-3)
     line = {

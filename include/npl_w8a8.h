@@ -154,16 +154,20 @@ int npl_rope_store_kv(const void* qkv, int ld_qkv, int T, int H, int Hkv, int D,
  * q fp16 [B, H, D] contiguous; caches fp16 [num_blocks, block_size, Hkv, D];
  * block_tables int32 [B, bt_stride] (first max_blocks entries used);
  * context_lens int32 [B]. out fp16 [B, H, D]. Softmax in fp32 over the
- * context; a row with context_len 0 (padded bucket row) yields zeros. The
- * workspace (npl_decode_attention_workspace_bytes) must be zero-filled once;
- * calls leave it zeroed.
+ * context; a row with context_len 0 (padded bucket row) yields zeros.
+ * With q_out/q_scale given, each row out[b] (H*D values) is also quantised
+ * per token as npl_quant_rows does: q_out int8 [B, H*D], q_scale fp32 [B]
+ * (the O projection's input, w8a8.py:106-115).
+ * D is 64 or 128; block_size a multiple of 64, or 8, 16 or 32. The workspace
+ * (npl_decode_attention_workspace_bytes) must be zero-filled once; calls
+ * leave it zeroed.
  */
 size_t npl_decode_attention_workspace_bytes(int B, int H, int D, int max_blocks, int block_size);
 int npl_paged_decode_attention(const void* q, int B, int H, int Hkv, int D, const void* k_cache,
                                const void* v_cache, int num_blocks, int block_size,
                                const int32_t* block_tables, int bt_stride, int max_blocks,
-                               const int32_t* context_lens, float scale, void* out, void* workspace,
-                               size_t workspace_bytes, void* stream);
+                               const int32_t* context_lens, float scale, void* out, int8_t* q_out_or_null,
+                               float* q_scale_or_null, void* workspace, size_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }

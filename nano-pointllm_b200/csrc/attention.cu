@@ -13,6 +13,8 @@
 #include <algorithm>
 #include <initializer_list>
 
+#include <cudaTypedefs.h>
+
 #include "npl_common.cuh"
 
 namespace npl {
@@ -28,6 +30,8 @@ __device__ __forceinline__ void flag_bad_index(int* status) {
 __global__ void store_kv_kernel(const __half* __restrict__ key, const __half* __restrict__ value, int ld_tok,
                                 int hkv_d, const int32_t* __restrict__ slots, __half* __restrict__ kc,
                                 __half* __restrict__ vc, long long num_slots, int* status) {
+  pdl_wait();
+  pdl_trigger();
   const int t = blockIdx.x;
   const long long slot = slots[t];
   if (slot < 0) return;  // padding token
@@ -46,74 +50,151 @@ __global__ void store_kv_kernel(const __half* __restrict__ key, const __half* __
 }
 
 // -------------------------------------------------------- RoPE + store
-// One CTA per token. Pair (d, d + D/2) of each q/k head:
+// Grid (token, head of q | k | v), D/2 threads. Pair (d, d + D/2) of a q/k
+// head:
 //   out[d]       = fp16(fp16(x1 * cos[d])       + fp16(-x2 * sin[d]))
 //   out[d + D/2] = fp16(fp16(x2 * cos[d + D/2]) + fp16( x1 * sin[d + D/2]))
 // (HF apply_rotary_pos_emb with rotate_half(x) = cat(-x2, x1), each torch
-// fp16 op rounded once).
+// fp16 op rounded once); v heads are copied to the cache unchanged.
 __global__ void rope_store_kernel(const __half* __restrict__ qkv, int ld_qkv, int H, int Hkv, int D,
                                   const __half* __restrict__ cos_t, const __half* __restrict__ sin_t,
                                   int max_position, const int64_t* __restrict__ positions,
                                   const int32_t* __restrict__ slots, __half* __restrict__ q_out,
                                   __half* __restrict__ kc, __half* __restrict__ vc, long long num_slots,
                                   int* status) {
-  const int t = blockIdx.x;
+  pdl_wait();
+  pdl_trigger();
+  const int t = blockIdx.x, head = blockIdx.y, d = threadIdx.x;
+  const int half_d = D / 2;
   const long long pos = positions[t];
   const long long slot = slots[t];
-  const __half* row = qkv + (size_t)t * ld_qkv;
-  const int half_d = D / 2;
   const bool pos_ok = pos >= 0 && pos < max_position;
   const bool slot_ok = slot >= 0 && slot < num_slots;
-  if (threadIdx.x == 0 && (!pos_ok || slot >= num_slots)) flag_bad_index(status);
+  if (head == 0 && d == 0 && (!pos_ok || slot >= num_slots)) flag_bad_index(status);
+  const __half* x = qkv + (size_t)t * ld_qkv + (size_t)head * D;
+  if (head >= H + Hkv) {  // v
+    if (slot_ok) {
+      __half* vd = vc + (slot * Hkv + (head - H - Hkv)) * D;
+      vd[d] = x[d];
+      vd[d + half_d] = x[d + half_d];
+    }
+    return;
+  }
   if (!pos_ok) return;
   const __half* c = cos_t + pos * D;
   const __half* s = sin_t + pos * D;
-  const int n_pairs = (H + Hkv) * half_d;
-  for (int i = threadIdx.x; i < n_pairs; i += blockDim.x) {
-    const int head = i / half_d, d = i - head * half_d;
-    const float x1 = __half2float(row[head * D + d]);
-    const float x2 = __half2float(row[head * D + d + half_d]);
-    const float a1 = __half2float(__float2half_rn(__fmul_rn(x1, __half2float(c[d]))));
-    const float b1 = __half2float(__float2half_rn(__fmul_rn(-x2, __half2float(s[d]))));
-    const float a2 = __half2float(__float2half_rn(__fmul_rn(x2, __half2float(c[d + half_d]))));
-    const float b2 = __half2float(__float2half_rn(__fmul_rn(x1, __half2float(s[d + half_d]))));
-    const __half o1 = __float2half_rn(__fadd_rn(a1, b1));
-    const __half o2 = __float2half_rn(__fadd_rn(a2, b2));
-    if (head < H) {
-      __half* qo = q_out + ((size_t)t * H + head) * D;
-      qo[d] = o1;
-      qo[d + half_d] = o2;
-    } else if (slot_ok) {
-      __half* kd = kc + (slot * Hkv + (head - H)) * D;
-      kd[d] = o1;
-      kd[d + half_d] = o2;
-    }
+  const float x1 = __half2float(x[d]);
+  const float x2 = __half2float(x[d + half_d]);
+  const float a1 = __half2float(__float2half_rn(__fmul_rn(x1, __half2float(c[d]))));
+  const float b1 = __half2float(__float2half_rn(__fmul_rn(-x2, __half2float(s[d]))));
+  const float a2 = __half2float(__float2half_rn(__fmul_rn(x2, __half2float(c[d + half_d]))));
+  const float b2 = __half2float(__float2half_rn(__fmul_rn(x1, __half2float(s[d + half_d]))));
+  const __half o1 = __float2half_rn(__fadd_rn(a1, b1));
+  const __half o2 = __float2half_rn(__fadd_rn(a2, b2));
+  __half* dst;
+  if (head < H) {
+    dst = q_out + ((size_t)t * H + head) * D;
+  } else {
+    if (!slot_ok) return;
+    dst = kc + (slot * Hkv + (head - H)) * D;
   }
-  if (slot_ok) {
-    const __half* v = row + (H + Hkv) * D;
-    __half* vd = vc + slot * Hkv * D;
-    for (int i = threadIdx.x; i < Hkv * D; i += blockDim.x) vd[i] = v[i];
-  }
+  dst[d] = o1;
+  dst[d + half_d] = o2;
 }
 
 // ------------------------------------------------- paged decode attention
-// Grid (splits, H, B); CTA = 4 warps; each half-warp (D = 128: 16 lanes x 8
-// dims) is a token stream with its own online-softmax state over the CTA's
-// chunk of the context. Streams merge in shared memory; each CTA writes a
-// partial (max, sum, acc[D]); the last CTA of (b, h) merges the splits and
-// writes the fp16 output.
-constexpr int kAttnThreads = 128;
-constexpr int kUnroll = 4;
+// Persistent kernel, at most one CTA per SM, 160 threads:
+//   warp 0     producer: takes work items from a global counter, looks up the
+//              block table and streams the item's K and V through a ring of
+//              64-token stages with TMA (3-D tensor maps over the cache viewed
+//              as [tokens][Hkv][D]; one box = min(64, block_size) tokens of
+//              one head)
+//   warps 1-4  consumers: D/8 lanes per token, 128/(D/8) token streams, each
+//              with its own online-softmax state over the item's tokens
+// A work item is (256-token chunk of the context, sequence b, head h). At the
+// end of an item the streams are merged into a partial (max, sum, acc[D]) in
+// the workspace; the CTA that completes the last chunk of (b, h) merges the
+// partials into out[b, h]; with q_out given, the CTA that completes the last
+// head of b quantises the attention row of b per token (w8a8.py:106-115),
+// which is the input of the O projection.
+constexpr int kAttnTok = 64;
+constexpr int kAttnStages = 2;
+constexpr int kAttnCtasPerSm = 3;  // 3 x ~66 KB of shared memory per SM
+constexpr int kAttnChunk = 256;
+constexpr int kAttnConsumers = 128;
+constexpr int kAttnThreads = 32 + kAttnConsumers;
 constexpr float kNegBig = -1.0e30f;
 
 template <int D>
-struct AttnCfg {
-  static constexpr int kLanesPerTok = D / 8;               // 16 B per lane
-  static constexpr int kStreams = kAttnThreads / kLanesPerTok;
+struct alignas(128) AttnSmem {
+  static constexpr int kStreams = kAttnConsumers / (D / 8);
+  __half k[kAttnStages][kAttnTok * D];
+  __half v[kAttnStages][kAttnTok * D];
+  __half q[kAttnStages][D];  // the item's query, sent with its first stage
+  float acc[kStreams][D];
+  float m[kStreams];
+  float l[kStreams];
+  float red[4];
+  uint64_t full[kAttnStages];
+  uint64_t empty[kAttnStages];
+  int4 meta[kAttnStages];  // item (-1: no more work), stage in item, valid tokens, last stage of item
+  int last_bh;
+  int last_row;
 };
 
-__device__ __forceinline__ void load8(const __half* p, float (&v)[8]) {
-  const uint4 x = __ldcs(reinterpret_cast<const uint4*>(p));
+struct AttnArgs {
+  const __half* q;
+  int B, H, Hkv;
+  int num_blocks, block_size, box_tok;
+  const int32_t* bt;
+  int bt_stride, max_blocks;
+  const int32_t* ctx_lens;
+  float scale;
+  int n_chunks, n_items;
+  __half* out;
+  int8_t* q_out;
+  float* q_scale;
+  float* part_ml;    // [B*H*n_chunks][2]
+  float* part_acc;   // [B*H*n_chunks][D]
+  int32_t* cnt_bh;   // [B*H]
+  int32_t* cnt_row;  // [B]
+  int32_t* work;     // [2]: next item, CTAs done
+  int* status;
+};
+
+__device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map, int c0, int c1, int c2,
+                                            uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ void consumer_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// 1-D bulk copy global -> shared, completion counted on `bar` (16-byte multiple).
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(smem_dst)),
+               "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+// Counter increment with acquire-release semantics at GPU scope: the CTA's
+// earlier writes (ordered before this thread by a barrier) are visible to
+// whoever observes the new value, and writes observed here are visible after.
+__device__ __forceinline__ int atomic_add_acq_rel(int32_t* p, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
+__device__ __forceinline__ int attn_ctx(const AttnArgs& p, int b) {
+  return min(max(0, p.ctx_lens[b]), p.max_blocks * p.block_size);
+}
+
+__device__ __forceinline__ void unpack8(const uint4& x, float (&v)[8]) {
   const __half2* h = reinterpret_cast<const __half2*>(&x);
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
@@ -124,151 +205,311 @@ __device__ __forceinline__ void load8(const __half* p, float (&v)[8]) {
 }
 
 template <int D>
-__global__ void __launch_bounds__(kAttnThreads)
-    decode_attn_kernel(const __half* __restrict__ q, int H, int Hkv, const __half* __restrict__ kc,
-                       const __half* __restrict__ vc, int num_blocks, int block_size,
-                       const int32_t* __restrict__ bt, int bt_stride, int max_blocks,
-                       const int32_t* __restrict__ ctx_lens, float scale, int chunk, __half* __restrict__ out,
-                       float* __restrict__ part_ml, float* __restrict__ part_acc, int32_t* __restrict__ counters,
-                       int* status) {
-  using C = AttnCfg<D>;
-  const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int n_splits = gridDim.x;
-  // a context longer than the block table row is clamped (and flagged)
-  const int ctx_raw = ctx_lens[b];
-  const int ctx = min(max(0, ctx_raw), max_blocks * block_size);
-  if (ctx != max(0, ctx_raw) && split == 0 && h == 0 && threadIdx.x == 0) flag_bad_index(status);
-  const int active = max(1, (ctx + chunk - 1) / chunk);
-  if (split >= active) return;
-  const int kvh = h / (H / Hkv);
-  const int tid = threadIdx.x;
-  const int stream = tid / C::kLanesPerTok;
-  const int sl = tid % C::kLanesPerTok;  // lane within the token stream
-  const unsigned grp_mask = C::kLanesPerTok == 32 ? 0xffffffffu
-                                                  : (((1u << C::kLanesPerTok) - 1) << ((tid & 31) & ~(C::kLanesPerTok - 1)));
-
-  float qv[8];
-  load8(q + ((size_t)b * H + h) * D + sl * 8, qv);
-  const float qscale = scale * 1.4426950408889634f;  // scores in log2 units
+__device__ void attn_item_end(const AttnArgs& p, AttnSmem<D>& s, int ct, int stream, int sl, int b, int h, int chunk,
+                              float m, float l, const float (&acc)[8]) {
+  constexpr int S = AttnSmem<D>::kStreams;
+  const int bh = b * p.H + h;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) qv[i] *= qscale;
-
-  float m = kNegBig, l = 0.f, acc[8];
+  for (int i = 0; i < 8; ++i) s.acc[stream][sl * 8 + i] = acc[i];
+  if (sl == 0) {
+    s.m[stream] = m;
+    s.l[stream] = l;
+  }
+  consumer_bar();
+  const size_t pidx = (size_t)bh * p.n_chunks + chunk;
+  if (ct < D) {
+    float mm = kNegBig;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-
-  const int t_begin = split * chunk;
-  const int t_end = min(ctx, t_begin + chunk);
-  const size_t tok_stride = (size_t)Hkv * D;
-  const int32_t* table = bt + (size_t)b * bt_stride;
-  for (int t0 = t_begin + stream; t0 < t_end; t0 += C::kStreams * kUnroll) {
-    float kv[kUnroll][8], vv[kUnroll][8];
-    bool valid[kUnroll];
+    for (int i = 0; i < S; ++i) mm = fmaxf(mm, s.m[i]);
+    float ll = 0.f, aa = 0.f;
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
-      const int t = t0 + u * C::kStreams;
-      valid[u] = t < t_end;
-      if (valid[u]) {
-        const int blk = table[t / block_size];
-        if (blk < 0 || blk >= num_blocks) {
-          valid[u] = false;
-          flag_bad_index(status);
-        } else {
-          const size_t off = ((size_t)blk * block_size + (t % block_size)) * tok_stride + (size_t)kvh * D + sl * 8;
-          load8(kc + off, kv[u]);
-          load8(vc + off, vv[u]);
+    for (int i = 0; i < S; ++i) {
+      const float w = exp2f(s.m[i] - mm);
+      ll += s.l[i] * w;
+      aa += s.acc[i][ct] * w;
+    }
+    __stcg(p.part_acc + pidx * D + ct, aa);
+    if (ct == 0) {
+      __stcg(p.part_ml + pidx * 2, mm);
+      __stcg(p.part_ml + pidx * 2 + 1, ll);
+    }
+  }
+  consumer_bar();
+  const int active = max(1, (attn_ctx(p, b) + kAttnChunk - 1) / kAttnChunk);
+  if (ct == 0) s.last_bh = (atomic_add_acq_rel(p.cnt_bh + bh, 1) + 1 == active);
+  consumer_bar();
+  if (s.last_bh) {
+    if (ct < D) {
+      float mm = kNegBig;
+      for (int c = 0; c < active; ++c) mm = fmaxf(mm, __ldcg(p.part_ml + ((size_t)bh * p.n_chunks + c) * 2));
+      float ll = 0.f, aa = 0.f;
+      for (int c = 0; c < active; ++c) {
+        const size_t pi = (size_t)bh * p.n_chunks + c;
+        const float w = exp2f(__ldcg(p.part_ml + pi * 2) - mm);
+        ll += __ldcg(p.part_ml + pi * 2 + 1) * w;
+        aa += __ldcg(p.part_acc + pi * D + ct) * w;
+        __stcg(p.part_acc + pi * D + ct, 0.f);
+      }
+      p.out[(size_t)bh * D + ct] = __float2half_rn(ll > 0.f ? aa / ll : 0.f);
+    }
+    consumer_bar();  // every merge read of part_ml is done before it is cleared
+    for (int i = ct; i < 2 * active; i += kAttnConsumers) __stcg(p.part_ml + (size_t)bh * p.n_chunks * 2 + i, 0.f);
+    if (ct == 0) p.cnt_bh[bh] = 0;
+    if (p.q_out) {
+      consumer_bar();
+      if (ct == 0) s.last_row = (atomic_add_acq_rel(p.cnt_row + b, 1) + 1 == p.H);
+      consumer_bar();
+      if (s.last_row) {
+        // per-token quantisation of the attention row of b (as npl_quant_rows)
+        const int n = p.H * D;
+        const __half* row = p.out + (size_t)b * n;
+        float amax = 0.f;
+        for (int i = ct * 8; i < n; i += kAttnConsumers * 8) {
+          float v[8];
+          unpack8(__ldcg(reinterpret_cast<const uint4*>(row + i)), v);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(v[j]));
+        }
+        amax = warp_max(amax);
+        if ((ct & 31) == 0) s.red[ct >> 5] = amax;
+        consumer_bar();
+        amax = fmaxf(fmaxf(s.red[0], s.red[1]), fmaxf(s.red[2], s.red[3]));
+        const float sc = scale_from_absmax(amax);
+        int8_t* qrow = p.q_out + (size_t)b * n;
+        for (int i = ct * 8; i < n; i += kAttnConsumers * 8) {
+          float v[8];
+          unpack8(__ldcg(reinterpret_cast<const uint4*>(row + i)), v);
+          uint2 u;
+          uint32_t* w = reinterpret_cast<uint32_t*>(&u);
+          w[0] = w[1] = 0;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) w[j / 4] |= (uint32_t)(quantize_one(v[j], sc) & 0xff) << (8 * (j % 4));
+          *reinterpret_cast<uint2*>(qrow + i) = u;
+        }
+        if (ct == 0) {
+          p.q_scale[b] = sc;
+          p.cnt_row[b] = 0;
         }
       }
     }
-    float sc[kUnroll];
-    float mnew = m;
-#pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
-      float d = 0.f;
-      if (valid[u]) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) d = fmaf(qv[i], kv[u][i], d);
-      }
-#pragma unroll
-      for (int o = C::kLanesPerTok / 2; o > 0; o >>= 1) d += __shfl_xor_sync(grp_mask, d, o);
-      sc[u] = valid[u] ? d : -INFINITY;
-      mnew = fmaxf(mnew, sc[u]);
-    }
-    const float alpha = exp2f(m - mnew);
-    l *= alpha;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) acc[i] *= alpha;
-#pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
-      const float pu = exp2f(sc[u] - mnew);
-      l += pu;
-      if (valid[u]) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) acc[i] = fmaf(pu, vv[u][i], acc[i]);
-      }
-    }
-    m = mnew;
   }
-
-  // merge the token streams of this CTA
-  __shared__ float s_acc[C::kStreams][D];
-  __shared__ float s_m[C::kStreams], s_l[C::kStreams];
-  __shared__ int s_last;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) s_acc[stream][sl * 8 + i] = acc[i];
-  if (sl == 0) {
-    s_m[stream] = m;
-    s_l[stream] = l;
-  }
-  __syncthreads();
-  const size_t ph = ((size_t)b * H + h);
-  const size_t pidx = ph * n_splits + split;
-  if (tid < D) {
-    float mm = kNegBig;
-    for (int s = 0; s < C::kStreams; ++s) mm = fmaxf(mm, s_m[s]);
-    float ll = 0.f, aa = 0.f;
-    for (int s = 0; s < C::kStreams; ++s) {
-      const float w = exp2f(s_m[s] - mm);
-      ll += s_l[s] * w;
-      aa += s_acc[s][tid] * w;
-    }
-    __stcg(part_acc + pidx * D + tid, aa);
-    if (tid == 0) {
-      __stcg(part_ml + pidx * 2, mm);
-      __stcg(part_ml + pidx * 2 + 1, ll);
-    }
-  }
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) {
-    const int prev = atomicAdd(counters + ph, 1);
-    s_last = (prev + 1 == active);
-    __threadfence();
-  }
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  // last CTA of (b, h): merge `active` splits
-  if (tid < D) {
-    float mm = kNegBig;
-    for (int s = 0; s < active; ++s) mm = fmaxf(mm, __ldcg(part_ml + (ph * n_splits + s) * 2));
-    float ll = 0.f, aa = 0.f;
-    for (int s = 0; s < active; ++s) {
-      const size_t pi = ph * n_splits + s;
-      const float w = exp2f(__ldcg(part_ml + pi * 2) - mm);
-      ll += __ldcg(part_ml + pi * 2 + 1) * w;
-      aa += __ldcg(part_acc + pi * D + tid) * w;
-      __stcg(part_acc + pi * D + tid, 0.f);
-    }
-    out[ph * D + tid] = __float2half_rn(ll > 0.f ? aa / ll : 0.f);
-  }
-  __syncthreads();  // every thread has read part_ml before it is cleared
-  // leave the whole workspace zero: its layout depends on the call's shape
-  for (int i = tid; i < 2 * active; i += kAttnThreads) __stcg(part_ml + ph * n_splits * 2 + i, 0.f);
-  if (tid == 0) counters[ph] = 0;
+  consumer_bar();  // stream state in shared memory is free for the next item
 }
 
-constexpr int kChunk = 256;
+template <int D>
+__global__ void __launch_bounds__(kAttnThreads, kAttnCtasPerSm)
+    decode_attn_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
+                       const AttnArgs p) {
+  extern __shared__ unsigned char smem_raw[];
+  AttnSmem<D>& s = *reinterpret_cast<AttnSmem<D>*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+  constexpr int LPT = D / 8;  // lanes per token: 16 B of the head vector each
+  constexpr int S = AttnSmem<D>::kStreams;
+  constexpr int kPerStream = kAttnTok / S;
+  constexpr int kU = kPerStream < 4 ? kPerStream : 4;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    prefetch_tensormap(&tmap_k);
+    prefetch_tensormap(&tmap_v);
+    for (int i = 0; i < kAttnStages; ++i) {
+      mbar_init(&s.full[i], 1);
+      mbar_init(&s.empty[i], kAttnConsumers / 32);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+  pdl_trigger();
+  pdl_wait();
+
+  if (warp == 0) {
+    // ---------------------------------------------------------- producer
+    if (lane == 0) {
+      const uint64_t pol = policy_evict_first();
+      const int bh_count = p.B * p.H;
+      const int groups = p.H / p.Hkv;
+      const uint32_t piece_bytes = (uint32_t)p.box_tok * D * sizeof(__half);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      while (ok) {
+        const int item = atomicAdd(p.work, 1);
+        if (item >= p.n_items) break;
+        const int chunk = item / bh_count, bh = item % bh_count;
+        const int b = bh / p.H, h = bh % p.H, kvh = h / groups;
+        const int ctx = attn_ctx(p, b);
+        const int t0 = chunk * kAttnChunk;
+        if (t0 >= ctx && chunk > 0) continue;  // past the context: nothing to do
+        const int t_end = min(ctx, t0 + kAttnChunk);
+        const int n_st = max(1, (t_end - t0 + kAttnTok - 1) / kAttnTok);
+        const int32_t* table = p.bt + (size_t)b * p.bt_stride;
+        for (int st = 0; st < n_st && ok; ++st) {
+          const int tok0 = t0 + st * kAttnTok;
+          const int valid = max(0, min(kAttnTok, t_end - tok0));
+          const int n_pieces = (valid + p.box_tok - 1) / p.box_tok;
+          // block-table rows of the stage's pieces, read before waiting for a
+          // free slot so their latency overlaps the wait
+          int rows[kAttnTok / 8];
+          int n_ok = 0;
+#pragma unroll
+          for (int i = 0; i < kAttnTok / 8; ++i) {
+            rows[i] = -1;
+            if (i < n_pieces) {
+              const int tok = tok0 + i * p.box_tok;
+              const int blk = table[tok / p.block_size];
+              if (blk < 0 || blk >= p.num_blocks) {
+                atomicCAS(p.status, 0, kDevBadIndex);
+              } else {
+                rows[i] = blk * p.block_size + tok % p.block_size;
+                ++n_ok;
+              }
+            }
+          }
+          if (!mbar_wait(&s.empty[stage], phase ^ 1, p.status, NPL_DEV_TIMEOUT_TMA)) {
+            ok = false;
+            break;
+          }
+          s.meta[stage] = make_int4(item, st, valid, st == n_st - 1);
+          const uint32_t q_bytes = st == 0 ? (uint32_t)D * sizeof(__half) : 0u;
+          mbar_arrive_expect_tx(&s.full[stage], 2u * piece_bytes * (uint32_t)n_ok + q_bytes);
+          if (st == 0) bulk_load(s.q[stage], p.q + (size_t)bh * D, q_bytes, &s.full[stage]);
+#pragma unroll
+          for (int i = 0; i < kAttnTok / 8; ++i) {
+            if (rows[i] < 0) continue;
+            tma_load_3d(s.k[stage] + i * p.box_tok * D, &tmap_k, 0, kvh, rows[i], &s.full[stage], pol);
+            tma_load_3d(s.v[stage] + i * p.box_tok * D, &tmap_v, 0, kvh, rows[i], &s.full[stage], pol);
+          }
+          if (++stage == kAttnStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (ok && mbar_wait(&s.empty[stage], phase ^ 1, p.status, NPL_DEV_TIMEOUT_TMA)) {
+        s.meta[stage] = make_int4(-1, 0, 0, 0);
+        mbar_arrive(&s.full[stage]);
+        // the last CTA to run out of work resets the work counters
+        if (atomicAdd(p.work + 1, 1) + 1 == (int)gridDim.x) {
+          atomicExch(p.work, 0);
+          atomicExch(p.work + 1, 0);
+        }
+      }
+    }
+  } else {
+    // --------------------------------------------------------- consumers
+    const int ct = threadIdx.x - 32;
+    const int stream = ct / LPT, sl = ct % LPT;
+    const unsigned gmask = LPT == 32 ? 0xffffffffu : (((1u << LPT) - 1) << ((ct & 31) & ~(LPT - 1)));
+    const float qscale = p.scale * 1.4426950408889634f;  // scores in log2 units
+    float qv[8], acc[8];
+    float m = kNegBig, l = 0.f;
+    int stage = 0;
+    uint32_t phase = 0;
+    while (true) {
+      if (!mbar_wait(&s.full[stage], phase, p.status, NPL_DEV_TIMEOUT_EPILOGUE)) break;
+      const volatile int* mv = reinterpret_cast<volatile int*>(&s.meta[stage]);
+      const int4 meta = make_int4(mv[0], mv[1], mv[2], mv[3]);
+      if (meta.x < 0) break;
+      const int bh_count = p.B * p.H;
+      const int chunk = meta.x / bh_count, bh = meta.x % bh_count;
+      const int b = bh / p.H, h = bh % p.H;
+      if (meta.y == 0) {
+        unpack8(*reinterpret_cast<const uint4*>(s.q[stage] + sl * 8), qv);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          qv[i] *= qscale;
+          acc[i] = 0.f;
+        }
+        m = kNegBig;
+        l = 0.f;
+      }
+      const __half* ks = s.k[stage];
+      const __half* vs = s.v[stage];
+#pragma unroll
+      for (int j0 = 0; j0 < kPerStream; j0 += kU) {
+        float sc[kU];
+        float mnew = m;
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          const int t = stream + (j0 + u) * S;
+          float kv[8];
+          unpack8(*reinterpret_cast<const uint4*>(ks + t * D + sl * 8), kv);
+          float d = 0.f;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) d = fmaf(qv[i], kv[i], d);
+#pragma unroll
+          for (int o = LPT / 2; o > 0; o >>= 1) d += __shfl_xor_sync(gmask, d, o);
+          sc[u] = t < meta.z ? d : -INFINITY;
+          mnew = fmaxf(mnew, sc[u]);
+        }
+        const float alpha = exp2f(m - mnew);
+        l *= alpha;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[i] *= alpha;
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          const int t = stream + (j0 + u) * S;
+          if (t < meta.z) {
+            const float pu = exp2f(sc[u] - mnew);
+            l += pu;
+            float vv[8];
+            unpack8(*reinterpret_cast<const uint4*>(vs + t * D + sl * 8), vv);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[i] = fmaf(pu, vv[i], acc[i]);
+          }
+        }
+        m = mnew;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s.empty[stage]);
+      if (meta.w) attn_item_end<D>(p, s, ct, stream, sl, b, h, chunk, m, l, acc);
+      if (++stage == kAttnStages) {
+        stage = 0;
+        phase ^= 1;
+      }
+    }
+  }
+}
+
+// fp16 cache [num_blocks * block_size][Hkv][D] as a 3-D tensor map; box =
+// (D, 1 head, box_tok tokens).
+int make_cache_map(CUtensorMap* map, const void* base, int num_blocks, int block_size, int Hkv, int D, int box_tok) {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* f = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return fail(NPL_ERR_LAUNCH, "cuTensorMapEncodeTiled unavailable");
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  }
+  const cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)Hkv, (cuuint64_t)num_blocks * block_size};
+  const cuuint64_t strides[2] = {(cuuint64_t)D * 2, (cuuint64_t)Hkv * D * 2};
+  const cuuint32_t box[3] = {(cuuint32_t)D, 1, (cuuint32_t)box_tok};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(NPL_ERR_ARG, "cuTensorMapEncodeTiled (KV cache) failed (%d)", (int)r);
+  return NPL_OK;
+}
+
+struct AttnLayout {
+  size_t ml, acc, cnt_bh, cnt_row, work, total;
+};
+
+AttnLayout attn_layout(int B, int H, int D, int max_blocks, int block_size) {
+  auto al = [](size_t x) { return (x + 255) & ~size_t(255); };
+  const size_t n_chunks = std::max<size_t>(1, ((size_t)max_blocks * block_size + kAttnChunk - 1) / kAttnChunk);
+  const size_t parts = (size_t)B * H * n_chunks;
+  AttnLayout l;
+  l.ml = 0;
+  l.acc = l.ml + al(parts * 2 * sizeof(float));
+  l.cnt_bh = l.acc + al(parts * D * sizeof(float));
+  l.cnt_row = l.cnt_bh + al((size_t)B * H * sizeof(int32_t));
+  l.work = l.cnt_row + al((size_t)B * sizeof(int32_t));
+  l.total = l.work + 256;
+  return l;
+}
 
 }  // namespace
 }  // namespace npl
@@ -286,11 +527,10 @@ extern "C" int npl_store_kv(const void* key, const void* value, int ld_tok, int 
   for (const void* p : std::initializer_list<const void*>{key, value, k_cache, v_cache})
     if (!aligned16(p)) return fail(NPL_ERR_ARG, "npl_store_kv: pointers must be 16-byte aligned");
   if (T == 0) return NPL_OK;
-  store_kv_kernel<<<T, 128, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __half*>(key), static_cast<const __half*>(value), ld_tok, Hkv * D, slot_mapping,
-      static_cast<__half*>(k_cache), static_cast<__half*>(v_cache), (long long)num_blocks * block_size,
-      device_status_ptr());
-  return launch_status("npl_store_kv");
+  return launch_pdl("npl_store_kv", store_kv_kernel, dim3(T), dim3(128), 0, static_cast<cudaStream_t>(stream),
+                    static_cast<const __half*>(key), static_cast<const __half*>(value), ld_tok, Hkv * D,
+                    slot_mapping, static_cast<__half*>(k_cache), static_cast<__half*>(v_cache),
+                    (long long)num_blocks * block_size, device_status_ptr());
 }
 
 extern "C" int npl_rope_store_kv(const void* qkv, int ld_qkv, int T, int H, int Hkv, int D, const void* cos_table,
@@ -300,70 +540,87 @@ extern "C" int npl_rope_store_kv(const void* qkv, int ld_qkv, int T, int H, int 
   if (int rc = check_device()) return rc;
   if (!qkv || !cos_table || !sin_table || !positions || !slot_mapping || !q_out || !k_cache || !v_cache)
     return fail(NPL_ERR_ARG, "npl_rope_store_kv: null pointer");
-  if (T < 0 || H <= 0 || Hkv <= 0 || H % Hkv || D <= 0 || D % 2 || ld_qkv < (H + 2 * Hkv) * D ||
+  if (T < 0 || H <= 0 || Hkv <= 0 || H % Hkv || D <= 0 || D % 2 || D > 2048 || ld_qkv < (H + 2 * Hkv) * D ||
       max_position <= 0 || num_blocks <= 0 || block_size <= 0)
     return fail(NPL_ERR_ARG, "npl_rope_store_kv: bad shape");
   if (T == 0) return NPL_OK;
-  rope_store_kernel<<<T, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __half*>(qkv), ld_qkv, H, Hkv, D, static_cast<const __half*>(cos_table),
-      static_cast<const __half*>(sin_table), max_position, positions, slot_mapping, static_cast<__half*>(q_out),
-      static_cast<__half*>(k_cache), static_cast<__half*>(v_cache), (long long)num_blocks * block_size,
-      device_status_ptr());
-  return launch_status("npl_rope_store_kv");
-}
-
-static int attn_splits(int max_blocks, int block_size) {
-  const long long max_ctx = (long long)max_blocks * block_size;
-  return (int)std::max<long long>(1, (max_ctx + kChunk - 1) / kChunk);
+  return launch_pdl("npl_rope_store_kv", rope_store_kernel, dim3(T, H + 2 * Hkv), dim3(D / 2), 0,
+                    static_cast<cudaStream_t>(stream), static_cast<const __half*>(qkv), ld_qkv, H, Hkv, D,
+                    static_cast<const __half*>(cos_table), static_cast<const __half*>(sin_table), max_position,
+                    positions, slot_mapping, static_cast<__half*>(q_out), static_cast<__half*>(k_cache),
+                    static_cast<__half*>(v_cache), (long long)num_blocks * block_size, device_status_ptr());
 }
 
 extern "C" size_t npl_decode_attention_workspace_bytes(int B, int H, int D, int max_blocks, int block_size) {
   if (B <= 0 || H <= 0 || D <= 0 || max_blocks <= 0 || block_size <= 0) return 0;
-  const size_t parts = (size_t)B * H * attn_splits(max_blocks, block_size);
-  const size_t ml = (parts * 2 * sizeof(float) + 255) & ~size_t(255);
-  const size_t acc = (parts * D * sizeof(float) + 255) & ~size_t(255);
-  const size_t cnt = ((size_t)B * H * sizeof(int32_t) + 255) & ~size_t(255);
-  return ml + acc + cnt;
+  return attn_layout(B, H, D, max_blocks, block_size).total;
 }
 
 extern "C" int npl_paged_decode_attention(const void* q, int B, int H, int Hkv, int D, const void* k_cache,
                                           const void* v_cache, int num_blocks, int block_size,
                                           const int32_t* block_tables, int bt_stride, int max_blocks,
-                                          const int32_t* context_lens, float scale, void* out, void* workspace,
-                                          size_t workspace_bytes, void* stream) {
+                                          const int32_t* context_lens, float scale, void* out, int8_t* q_out,
+                                          float* q_scale, void* workspace, size_t workspace_bytes, void* stream) {
   if (int rc = check_device()) return rc;
   if (!q || !k_cache || !v_cache || !block_tables || !context_lens || !out)
     return fail(NPL_ERR_ARG, "npl_paged_decode_attention: null pointer");
+  if ((q_out == nullptr) != (q_scale == nullptr))
+    return fail(NPL_ERR_ARG, "npl_paged_decode_attention: q_out and q_scale go together");
   if (B < 0 || H <= 0 || Hkv <= 0 || H % Hkv || num_blocks <= 0 || block_size <= 0 || max_blocks <= 0 ||
       bt_stride < max_blocks)
     return fail(NPL_ERR_ARG, "npl_paged_decode_attention: bad shape");
   if (D != 128 && D != 64) return fail(NPL_ERR_UNSUPPORTED, "npl_paged_decode_attention: head_dim %d (64 or 128)", D);
-  for (const void* p : std::initializer_list<const void*>{q, k_cache, v_cache})
-    if (!aligned16(p)) return fail(NPL_ERR_ARG, "npl_paged_decode_attention: pointers must be 16-byte aligned");
+  if (block_size < 8 || (block_size % kAttnTok && kAttnTok % block_size))
+    return fail(NPL_ERR_UNSUPPORTED,
+                "npl_paged_decode_attention: block_size %d (a multiple of 64, or 8, 16 or 32)", block_size);
+  for (const void* p : std::initializer_list<const void*>{q, k_cache, v_cache, out, (const void*)q_out})
+    if (p && !aligned16(p)) return fail(NPL_ERR_ARG, "npl_paged_decode_attention: pointers must be 16-byte aligned");
   if (B == 0) return NPL_OK;
-  const size_t need = npl_decode_attention_workspace_bytes(B, H, D, max_blocks, block_size);
-  if (!workspace || workspace_bytes < need || !aligned16(workspace))
-    return fail(NPL_ERR_ARG, "npl_paged_decode_attention: workspace of %zu bytes required", need);
-  const int splits = attn_splits(max_blocks, block_size);
-  const size_t parts = (size_t)B * H * splits;
+  const AttnLayout lay = attn_layout(B, H, D, max_blocks, block_size);
+  if (!workspace || workspace_bytes < lay.total || !aligned16(workspace))
+    return fail(NPL_ERR_ARG, "npl_paged_decode_attention: workspace of %zu bytes required", lay.total);
+  const int box_tok = std::min(kAttnTok, block_size);
+  CUtensorMap tk, tv;
+  if (int rc = make_cache_map(&tk, k_cache, num_blocks, block_size, Hkv, D, box_tok)) return rc;
+  if (int rc = make_cache_map(&tv, v_cache, num_blocks, block_size, Hkv, D, box_tok)) return rc;
   char* ws = static_cast<char*>(workspace);
-  float* part_ml = reinterpret_cast<float*>(ws);
-  float* part_acc = reinterpret_cast<float*>(ws + ((parts * 2 * sizeof(float) + 255) & ~size_t(255)));
-  int32_t* counters = reinterpret_cast<int32_t*>(reinterpret_cast<char*>(part_acc) +
-                                                 ((parts * D * sizeof(float) + 255) & ~size_t(255)));
-  dim3 grid(splits, H, B);
+  AttnArgs p{};
+  p.q = static_cast<const __half*>(q);
+  p.B = B;
+  p.H = H;
+  p.Hkv = Hkv;
+  p.num_blocks = num_blocks;
+  p.block_size = block_size;
+  p.box_tok = box_tok;
+  p.bt = block_tables;
+  p.bt_stride = bt_stride;
+  p.max_blocks = max_blocks;
+  p.ctx_lens = context_lens;
+  p.scale = scale;
+  p.n_chunks = std::max(1, (max_blocks * block_size + kAttnChunk - 1) / kAttnChunk);
+  p.n_items = p.n_chunks * B * H;
+  p.out = static_cast<__half*>(out);
+  p.q_out = q_out;
+  p.q_scale = q_scale;
+  p.part_ml = reinterpret_cast<float*>(ws + lay.ml);
+  p.part_acc = reinterpret_cast<float*>(ws + lay.acc);
+  p.cnt_bh = reinterpret_cast<int32_t*>(ws + lay.cnt_bh);
+  p.cnt_row = reinterpret_cast<int32_t*>(ws + lay.cnt_row);
+  p.work = reinterpret_cast<int32_t*>(ws + lay.work);
+  p.status = device_status_ptr();
+  const int sms = num_sms();
+  const int grid = std::min(kAttnCtasPerSm * (sms > 0 ? sms : 148), p.n_items);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (D == 128)
-    decode_attn_kernel<128><<<grid, kAttnThreads, 0, st>>>(
-        static_cast<const __half*>(q), H, Hkv, static_cast<const __half*>(k_cache), static_cast<const __half*>(v_cache),
-        num_blocks, block_size, block_tables, bt_stride, max_blocks, context_lens, scale, kChunk,
-        static_cast<__half*>(out),
-        part_ml, part_acc, counters, device_status_ptr());
-  else
-    decode_attn_kernel<64><<<grid, kAttnThreads, 0, st>>>(
-        static_cast<const __half*>(q), H, Hkv, static_cast<const __half*>(k_cache), static_cast<const __half*>(v_cache),
-        num_blocks, block_size, block_tables, bt_stride, max_blocks, context_lens, scale, kChunk,
-        static_cast<__half*>(out),
-        part_ml, part_acc, counters, device_status_ptr());
-  return launch_status("npl_paged_decode_attention");
+  if (D == 128) {
+    const int smem = (int)sizeof(AttnSmem<128>) + 128;
+    if (cudaFuncSetAttribute(decode_attn_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+      return launch_status("npl_paged_decode_attention: smem attribute");
+    return launch_pdl("npl_paged_decode_attention", decode_attn_kernel<128>, dim3(grid), dim3(kAttnThreads),
+                      (size_t)smem, st, tk, tv, p);
+  }
+  const int smem = (int)sizeof(AttnSmem<64>) + 128;
+  if (cudaFuncSetAttribute(decode_attn_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    return launch_status("npl_paged_decode_attention: smem attribute");
+  return launch_pdl("npl_paged_decode_attention", decode_attn_kernel<64>, dim3(grid), dim3(kAttnThreads),
+                    (size_t)smem, st, tk, tv, p);
 }

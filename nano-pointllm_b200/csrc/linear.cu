@@ -211,26 +211,45 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = s.tmem_base;
+  pdl_trigger();  // the next kernel may start launching its CTAs
 
   if (warp == 0) {
     // ---------------------------------------------------------- TMA producer
     if (lane == 0) {
       const uint64_t pol_w = policy_evict_first();
       const uint64_t pol_x = policy_evict_last();
+      // Weights do not depend on earlier kernels: the weight tiles of the
+      // first ring stages are requested before waiting for the previous
+      // kernel; the token tiles (its output) only after.
+      int pre = 0;
+      {
+        SegmentIter it(p);
+        int tile, kb0, kb1;
+        while (pre < STAGES && it.next(tile, kb0, kb1)) {
+          const int n_tile = tile % p.n_tiles;
+          for (int kb = kb0; kb < kb1 && pre < STAGES; ++kb, ++pre) {
+            mbar_arrive_expect_tx(&s.full[pre], kStageBytes);
+            tma_load_2d(s.a[pre], &tmap_w, kb * kBlockK, n_tile * kTileN, &s.full[pre], pol_w);
+          }
+        }
+      }
+      uint32_t outstanding = pre >= 32 ? 0xffffffffu : ((1u << pre) - 1);  // stages holding a load
+      pdl_wait();
       SegmentIter it(p);
-      int tile, kb0, kb1, stage = 0;
+      int tile, kb0, kb1, stage = 0, unit = 0;
       uint32_t phase = 0;
-      uint32_t outstanding = 0;  // bit i: stage i holds a load not known complete
       bool ok = true;
       while (ok && it.next(tile, kb0, kb1)) {
         const int m_tile = tile / p.n_tiles, n_tile = tile % p.n_tiles;
-        for (int kb = kb0; kb < kb1; ++kb) {
-          if (!mbar_wait(&s.empty[stage], phase ^ 1, p.status, NPL_DEV_TIMEOUT_TMA)) {
-            ok = false;
-            break;
+        for (int kb = kb0; kb < kb1; ++kb, ++unit) {
+          if (unit >= pre) {
+            if (!mbar_wait(&s.empty[stage], phase ^ 1, p.status, NPL_DEV_TIMEOUT_TMA)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&s.full[stage], kStageBytes);
+            tma_load_2d(s.a[stage], &tmap_w, kb * kBlockK, n_tile * kTileN, &s.full[stage], pol_w);
           }
-          mbar_arrive_expect_tx(&s.full[stage], kStageBytes);
-          tma_load_2d(s.a[stage], &tmap_w, kb * kBlockK, n_tile * kTileN, &s.full[stage], pol_w);
           tma_load_2d(s.b[stage], &tmap_x, kb * kBlockK, m_tile * NT, &s.full[stage], pol_x);
           outstanding |= 1u << stage;
           if (++stage == STAGES) {
@@ -239,6 +258,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
+
       // Drain: every issued load must land before the CTA's shared memory is
       // released. A stage's last load used parity (phase of that issue).
       for (int i = 0; i < STAGES; ++i) {
@@ -293,6 +313,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // -------------------------------------------------------------- epilogue
     const int quarter = warp & 3;  // TMEM lanes this warp may access
     const int row = quarter * 32 + lane;
+    pdl_wait();
     SegmentIter it(p);
     int tile, kb0, kb1, seg = 0;
     while (it.next(tile, kb0, kb1)) {
@@ -429,8 +450,7 @@ int launch_linear(const CUtensorMap& tw, const CUtensorMap& tx, LinearArgs& p, c
     configured = true;
   }
   const long long grid = std::min<long long>(max_grid(), p.total_units);
-  kern<<<(unsigned)grid, kThreads, smem, st>>>(tw, tx, p);
-  return launch_status("npl_w8a8_linear");
+  return launch_pdl("npl_w8a8_linear", kern, dim3((unsigned)grid), dim3(kThreads), (size_t)smem, st, tw, tx, p);
 }
 
 }  // namespace
@@ -499,11 +519,14 @@ extern "C" int npl_w8a8_linear(const int8_t* qa, int lda, const float* sa, const
   if (int rc = make_map(&tw, qw, N, K, ldw, kTileN)) return rc;
   if (int rc = make_map(&tx, qa, M, K, lda, nt)) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // Decode tiles (NT <= 64) keep the ring near 100 KB so that the next
+  // kernel's CTA fits beside this one on an SM and starts its weight loads
+  // while this one finishes (programmatic dependent launch).
   switch (nt) {
-    case 8: return launch_linear<8, 12>(tw, tx, p, st);
-    case 16: return launch_linear<16, 11>(tw, tx, p, st);
-    case 32: return launch_linear<32, 10>(tw, tx, p, st);
-    case 64: return launch_linear<64, 8>(tw, tx, p, st);
+    case 8: return launch_linear<8, 6>(tw, tx, p, st);
+    case 16: return launch_linear<16, 6>(tw, tx, p, st);
+    case 32: return launch_linear<32, 5>(tw, tx, p, st);
+    case 64: return launch_linear<64, 4>(tw, tx, p, st);
     case 128: return launch_linear<128, 6>(tw, tx, p, st);
     default: return launch_linear<256, 4>(tw, tx, p, st);
   }

@@ -29,7 +29,36 @@ int check_device();                    // NPL_OK on an sm_100 device
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Launch with programmatic dependent launch (PDL): the kernel may start while
+// the previous kernel on the stream is finishing; it must execute pdl_wait()
+// before touching any global memory the previous kernels read or write
+// (constant weights excepted), and calls pdl_trigger() to let the next kernel
+// start early in turn.
+template <typename... KArgs, typename... Args>
+int launch_pdl(const char* what, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+               Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+  if (e != cudaSuccess) {
+    (void)cudaGetLastError();
+    return fail(NPL_ERR_LAUNCH, "%s: %s", what, cudaGetErrorString(e));
+  }
+  return NPL_OK;
+}
+
 // ------------------------------------------------------------- device side
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // Error word shared by all kernels of the library on this device. A kernel
 // that gives up a bounded wait stores its NPL_DEV_* code here; the host reads
 // it with npl_device_status().

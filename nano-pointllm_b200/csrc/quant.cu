@@ -64,6 +64,8 @@ __global__ void __launch_bounds__(kQuantThreads) quant_rows_kernel(const T* __re
                                                                    float* __restrict__ scale) {
   __shared__ float red[32];
   constexpr int V = Vec<T>::N;
+  pdl_wait();
+  pdl_trigger();
   const T* row = x + (size_t)blockIdx.x * ldx;
   float amax = 0.f;
   for (int c = threadIdx.x * V; c < cols; c += kQuantThreads * V) {
@@ -96,6 +98,8 @@ __global__ void __launch_bounds__(kQuantThreads)
   __half* srow = reinterpret_cast<__half*>(smem_raw);
   __shared__ double dred[32];
   __shared__ float fred[32];
+  pdl_wait();
+  pdl_trigger();
   const size_t base = (size_t)blockIdx.x * cols;
 
   // 1. s = x (+ residual, fp16 add), sum of squares in fp64 (squares of fp16
@@ -171,12 +175,12 @@ extern "C" int npl_quant_rows(const void* x, int x_dtype, int rows, int cols, in
   if (rows == 0) return NPL_OK;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (x_dtype == NPL_F32)
-    quant_rows_kernel<float><<<rows, kQuantThreads, 0, st>>>(static_cast<const float*>(x), cols, ldx, q, ldq, scale);
-  else if (x_dtype == NPL_F16)
-    quant_rows_kernel<__half><<<rows, kQuantThreads, 0, st>>>(static_cast<const __half*>(x), cols, ldx, q, ldq, scale);
-  else
-    return fail(NPL_ERR_ARG, "npl_quant_rows: x_dtype must be NPL_F32 or NPL_F16");
-  return launch_status("npl_quant_rows");
+    return launch_pdl("npl_quant_rows", quant_rows_kernel<float>, dim3(rows), dim3(kQuantThreads), 0, st,
+                      static_cast<const float*>(x), cols, ldx, q, ldq, scale);
+  if (x_dtype == NPL_F16)
+    return launch_pdl("npl_quant_rows", quant_rows_kernel<__half>, dim3(rows), dim3(kQuantThreads), 0, st,
+                      static_cast<const __half*>(x), cols, ldx, q, ldq, scale);
+  return fail(NPL_ERR_ARG, "npl_quant_rows: x_dtype must be NPL_F32 or NPL_F16");
 }
 
 extern "C" int npl_rmsnorm_quant(const void* x, const void* residual, const void* weight, float eps, int rows,
@@ -195,8 +199,8 @@ extern "C" int npl_rmsnorm_quant(const void* x, const void* residual, const void
         cudaSuccess)
       return launch_status("npl_rmsnorm_quant: smem attribute");
   }
-  rmsnorm_quant_kernel<<<rows, kQuantThreads, smem, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __half*>(x), static_cast<const __half*>(residual), static_cast<const __half*>(weight), eps,
-      cols, static_cast<__half*>(sum_out), static_cast<__half*>(normed_out), q, scale);
-  return launch_status("npl_rmsnorm_quant");
+  return launch_pdl("npl_rmsnorm_quant", rmsnorm_quant_kernel, dim3(rows), dim3(kQuantThreads), smem,
+                    static_cast<cudaStream_t>(stream), static_cast<const __half*>(x),
+                    static_cast<const __half*>(residual), static_cast<const __half*>(weight), eps, cols,
+                    static_cast<__half*>(sum_out), static_cast<__half*>(normed_out), q, scale);
 }

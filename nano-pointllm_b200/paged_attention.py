@@ -69,11 +69,13 @@ def decode_attention_workspace(device: torch.device, b: int, h: int, d: int, max
 def paged_decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
                            block_tables: torch.Tensor, context_lens: torch.Tensor, scale: float,
                            num_kv_groups: int, block_n: int | None = None,
-                           out: torch.Tensor | None = None) -> torch.Tensor:
+                           out: torch.Tensor | None = None, quant_out: tuple | None = None) -> torch.Tensor:
     """Decode-only paged attention (q_len = 1): q fp16 [B, H, D] -> [B, H, D].
 
     ``block_n`` is accepted for signature compatibility with the reference
     (its Triton tile size); the kernel chooses its own context split.
+    ``quant_out = (q8 int8 [B, H*D], scale fp32 [B])`` also receives the
+    per-token int8 quantisation of each output row (the O projection input).
     """
     del block_n
     _check_cache(k_cache, v_cache)
@@ -90,8 +92,9 @@ def paged_decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torc
         raise ValueError("block_tables and context_lens must be int32")
     max_blocks = block_tables.shape[1]
     ws = decode_attention_workspace(q.device, b, h, d, max_blocks, bs)
+    q8, qs = quant_out if quant_out is not None else (None, None)
     L.check(L.lib.npl_paged_decode_attention(
         q.data_ptr(), b, h, hkv, d, k_cache.data_ptr(), v_cache.data_ptr(), nb, bs, block_tables.data_ptr(),
-        block_tables.stride(0), max_blocks, context_lens.data_ptr(), float(scale), out.data_ptr(), ws.data_ptr(),
-        ws.numel(), L.stream_ptr(q.device)))
+        block_tables.stride(0), max_blocks, context_lens.data_ptr(), float(scale), out.data_ptr(), L.ptr(q8),
+        L.ptr(qs), ws.data_ptr(), ws.numel(), L.stream_ptr(q.device)))
     return out

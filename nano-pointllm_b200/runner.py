@@ -17,9 +17,9 @@ Every Linear (packed QKV, O, packed gate/up, down, LM head) is W8A8: int8
 weights quantised once per output channel, int8 activations quantised per
 token, int32 accumulation on the tensor cores, dequant fused into the linear's
 epilogue together with the residual add (O, down) and SiLU(gate) * up. The
-decode step per layer is 10 kernels of libnpl_w8a8 and nothing else:
+decode step per layer is 9 kernels of libnpl_w8a8 and nothing else:
 
-  rmsnorm+quant -> QKV -> RoPE+store -> paged attention -> quant ->
+  rmsnorm+quant -> QKV -> RoPE+store -> paged attention(+quant) ->
   O(+residual) -> rmsnorm+quant -> gate/up(+SiLU*up) -> quant -> down(+residual)
 
 Prefill attention over multi-token rows uses torch SDPA per sequence on the
@@ -149,6 +149,21 @@ class W8A8LlamaRunner:
         return cls(shape, dict(hf_model.state_dict()), device=device, kv_pool=kv_pool)
 
     # ------------------------------------------------------------- layers
+    def _attention_q(self, layer: W8A8Layer, q: torch.Tensor, ctx: ForwardContext):
+        """q [T, H, D] (rotated) -> per-token int8 attention rows [T, H*D] +
+        fp32 scales [T] (the O projection's input). In decode steps the
+        quantisation is fused into the attention kernel."""
+        s = self.shape
+        t = q.shape[0]
+        if all(n == 1 for n in ctx.seq_lens):
+            q8 = torch.empty((t, s.heads * s.head_dim), dtype=torch.int8, device=q.device)
+            qs = torch.empty((t,), dtype=torch.float32, device=q.device)
+            PA.paged_decode_attention(q, layer.k_cache, layer.v_cache, ctx.block_tables, ctx.context_lens,
+                                      self.scale, s.heads // s.kv_heads, quant_out=(q8, qs))
+            return q8, qs
+        q8, qs = W.dynamic_per_token_quant(self._attention(layer, q, ctx))
+        return q8, qs.reshape(-1)
+
     def _attention(self, layer: W8A8Layer, q: torch.Tensor, ctx: ForwardContext) -> torch.Tensor:
         """q [T, H, D] (rotated) -> [T, H*D] fp16."""
         s = self.shape
@@ -202,9 +217,8 @@ class W8A8LlamaRunner:
         qkv = op("linear.qkv", W.linear_q, xq, xs, layer.qkv.qweight, layer.qkv.wscale)
         q = op("rope_store", PA.rope_store_kvcache, qkv, s.heads, s.kv_heads, s.head_dim, self.cos, self.sin,
                positions, ctx.slot_mapping, layer.k_cache, layer.v_cache)
-        attn = op("attention", self._attention, layer, q, ctx)
-        aq, asc = op("quant", W.dynamic_per_token_quant, attn)
-        h2 = op("linear.o", W.linear_q, aq, asc.reshape(-1), layer.o.qweight, layer.o.wscale,
+        aq, asc = op("attention", self._attention_q, layer, q, ctx)
+        h2 = op("linear.o", W.linear_q, aq, asc, layer.o.qweight, layer.o.wscale,
                 epilogue=L.EPI_RESIDUAL, residual=h)
         xq, xs, _ = op("rmsnorm_quant", rmsnorm_quant, h2, layer.post_norm, s.eps)
         act = op("linear.gate_up", W.linear_q, xq, xs, layer.gate_up.qweight, layer.gate_up.wscale,
