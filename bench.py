@@ -158,25 +158,27 @@ def step_metadata(torch, bt, step: int, device):
     return positions, slots, ctx
 
 
-def linear_bytes(m: int, n: int, k: int, out_cols: int, residual: bool) -> int:
-    """Algorithmic bytes of one W8A8 linear launch: int8 weight + int8
-    activations + fp32 scales + fp16 output (+ fp16 residual read)."""
-    return n * k + m * k + 4 * m + 4 * n + 2 * m * out_cols + (2 * m * out_cols if residual else 0)
+def linear_bytes(m: int, n: int, k: int, out_cols: int, residual: bool, fp16_x: bool) -> int:
+    """Algorithmic bytes of one W8A8 linear launch: int8 weight + fp32 weight
+    scales + activations (int8 + fp32 scales, or fp16 rows when the
+    quantisation is fused in) + fp16 output (+ fp16 residual read)."""
+    x = 2 * m * k if fp16_x else m * k + 4 * m
+    return n * k + 4 * n + x + 2 * m * out_cols + (2 * m * out_cols if residual else 0)
 
 
 def op_bytes(shape, name: str, ctx_len: int) -> int:
     m, h, i_, v = BATCH, shape.hidden, shape.intermediate, shape.vocab
     qkv_n = (shape.heads + 2 * shape.kv_heads) * shape.head_dim
-    if name == "linear.qkv":
-        return linear_bytes(m, qkv_n, h, qkv_n, False)
+    if name == "linear.qkv":  # q out, k/v written to the cache (+ positions, slots, cos/sin rows)
+        return linear_bytes(m, qkv_n, h, qkv_n, False, False)
     if name == "linear.o":
-        return linear_bytes(m, h, shape.heads * shape.head_dim, h, True)
+        return linear_bytes(m, h, shape.heads * shape.head_dim, h, True, False)
     if name == "linear.gate_up":
-        return linear_bytes(m, 2 * i_, h, i_, False)
+        return linear_bytes(m, 2 * i_, h, i_, False, False)
     if name == "linear.down":
-        return linear_bytes(m, h, i_, h, True)
+        return linear_bytes(m, h, i_, h, True, False)
     if name == "linear.lm_head":
-        return linear_bytes(m, v, h, v, False)
+        return linear_bytes(m, v, h, v, False, False)
     if name == "attention":
         # fp16 K and V of every context token of every head, q in, out
         return m * ctx_len * shape.kv_heads * shape.head_dim * 2 * 2 + 2 * 2 * m * shape.heads * shape.head_dim

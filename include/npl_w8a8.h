@@ -40,10 +40,16 @@ extern "C" {
 #define NPL_F32 0
 #define NPL_F16 1
 
-/* fused epilogues of npl_w8a8_linear */
+/* fused epilogues of npl_w8a8_linear / npl_w8a8_linear_ex */
 #define NPL_EPI_NONE 0     /* out = dequant(acc)                                  */
 #define NPL_EPI_RESIDUAL 1 /* out = fp16(fp16(dequant(acc)) + residual)           */
 #define NPL_EPI_SILU_MUL 2 /* gate/up rows tile-interleaved; out = silu(g) * u    */
+#define NPL_EPI_ROPE_KV 3  /* packed QKV: RoPE on q/k, q -> q_out, k/v -> cache (npl_w8a8_linear_ex) */
+
+/* activation operand of npl_w8a8_linear_ex */
+#define NPL_X_INT8 0        /* int8 [M, K] + fp32 per-token scales                       */
+#define NPL_X_F16_ABSMAX 1  /* fp16 [M, K] quantised in the kernel with a given absmax   */
+#define NPL_X_F16_RMSNORM 2 /* fp16 [M, K] RMSNorm-ed, then quantised in the kernel      */
 
 const char* npl_last_error_string(void);
 int npl_version(void);
@@ -105,6 +111,76 @@ int npl_w8a8_linear(const int8_t* qa, int lda, const float* sa, const int8_t* qw
                     const float* sw, const float* bias_or_null, int M, int N, int K, int epilogue,
                     const void* residual_or_null, int ld_res, void* out, int ld_out, int out_dtype,
                     int32_t* acc_out_or_null, void* workspace, size_t workspace_bytes, void* stream);
+
+/* RoPE + KV-cache store operands of NPL_EPI_ROPE_KV (see npl_rope_store_kv). */
+typedef struct npl_rope_kv {
+  const void* cos_table; /* fp16 [max_position, head_dim]                       */
+  const void* sin_table;
+  int max_position;
+  const int64_t* positions;     /* [M]                                        */
+  const int32_t* slot_mapping;  /* [M], negative = padding                    */
+  void* q_out;                  /* fp16 [M, heads, head_dim]                  */
+  void* k_cache;                /* fp16 [num_blocks, block_size, kv_heads, D] */
+  void* v_cache;
+  int num_blocks;
+  int block_size;
+  int heads;
+  int kv_heads;
+  int head_dim;
+} npl_rope_kv;
+
+/*
+ * npl_w8a8_linear with the layer math around a decode linear fused in.
+ * Activations (x_mode):
+ *   NPL_X_INT8         qa/lda/sa as npl_w8a8_linear.
+ *   NPL_X_F16_ABSMAX   x_f16 [M, K] (row stride ldx) quantised per token with
+ *                      scale = scale_from_absmax(x_absmax[m]) (float bits of
+ *                      max |x[m, :]|, e.g. an NPL_EPI_SILU_MUL absmax_out);
+ *                      the call zeroes x_absmax[0..M) after reading it.
+ *                      Same result as npl_quant_rows on x_f16.
+ *   NPL_X_F16_RMSNORM  x_f16 RMSNorm-ed with norm_weight/eps, then quantised:
+ *                      the same arithmetic as npl_rmsnorm_quant.
+ *   The fp16 modes take M <= 64 (decode batches).
+ * Epilogues: those of npl_w8a8_linear, plus
+ *   NPL_EPI_SILU_MUL with absmax_out: absmax_out[m] (float bits, zero before
+ *                      the call) receives max over the row of |out[m, :]|.
+ *   NPL_EPI_ROPE_KV    N = (heads + 2 kv_heads) * head_dim (packed q | k | v,
+ *                      head blocks multiples of 128 rows): q and k get RoPE
+ *                      exactly as npl_rope_store_kv; q -> rope.q_out; k and v
+ *                      -> the caches at slot_mapping (out is not written).
+ * Workspace: npl_linear_workspace_bytes(M, N, K), as npl_w8a8_linear.
+ * Replaces, for one decode step, lightweight_runner.py:239-245 + w8a8.py:
+ * 106-115 (RMSNorm and activation quantisation before the QKV, gate/up and
+ * LM-head linears), the down projection's activation quantisation, and
+ * paged_attention.py:1286-1294 (rotary_fn + store_kvcache).
+ */
+typedef struct npl_linear_args {
+  int x_mode;
+  const int8_t* qa;
+  int lda;
+  const float* sa;
+  const void* x_f16;
+  int ldx;
+  int32_t* x_absmax;
+  const void* norm_weight;
+  float eps;
+  const int8_t* qw;
+  int ldw;
+  const float* sw;
+  const float* bias;
+  int M, N, K;
+  int epilogue;
+  const void* residual;
+  int ld_res;
+  void* out;
+  int ld_out;
+  int out_dtype;
+  int32_t* acc_out;
+  int32_t* absmax_out;
+  npl_rope_kv rope;
+} npl_linear_args;
+
+int npl_w8a8_linear_ex(const npl_linear_args* args, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * npl_w8a8_linear without a workspace argument, for callers that cannot

@@ -27,11 +27,32 @@ NPL_F16 = 1
 EPI_NONE = 0
 EPI_RESIDUAL = 1
 EPI_SILU_MUL = 2
+EPI_ROPE_KV = 3
+
+X_INT8 = 0
+X_F16_ABSMAX = 1
+X_F16_RMSNORM = 2
 
 _P = ctypes.c_void_p
 _I = ctypes.c_int
 _F = ctypes.c_float
 _Z = ctypes.c_size_t
+
+class NplRopeKV(ctypes.Structure):
+    """npl_rope_kv (include/npl_w8a8.h)."""
+    _fields_ = [("cos_table", _P), ("sin_table", _P), ("max_position", _I), ("positions", _P),
+                ("slot_mapping", _P), ("q_out", _P), ("k_cache", _P), ("v_cache", _P), ("num_blocks", _I),
+                ("block_size", _I), ("heads", _I), ("kv_heads", _I), ("head_dim", _I)]
+
+
+class NplLinearArgs(ctypes.Structure):
+    """npl_linear_args (include/npl_w8a8.h)."""
+    _fields_ = [("x_mode", _I), ("qa", _P), ("lda", _I), ("sa", _P), ("x_f16", _P), ("ldx", _I),
+                ("x_absmax", _P), ("norm_weight", _P), ("eps", _F), ("qw", _P), ("ldw", _I), ("sw", _P),
+                ("bias", _P), ("M", _I), ("N", _I), ("K", _I), ("epilogue", _I), ("residual", _P), ("ld_res", _I),
+                ("out", _P), ("ld_out", _I), ("out_dtype", _I), ("acc_out", _P), ("absmax_out", _P),
+                ("rope", NplRopeKV)]
+
 
 # name -> (restype, argtypes); mirrors include/npl_w8a8.h
 SIGNATURES = {
@@ -42,6 +63,7 @@ SIGNATURES = {
     "npl_rmsnorm_quant": (_I, [_P, _P, _P, _F, _I, _I, _P, _P, _P, _P, _P]),
     "npl_linear_workspace_bytes": (_Z, [_I, _I, _I]),
     "npl_w8a8_linear": (_I, [_P, _I, _P, _P, _I, _P, _P, _I, _I, _I, _I, _P, _I, _P, _I, _I, _P, _P, _Z, _P]),
+    "npl_w8a8_linear_ex": (_I, [ctypes.POINTER(NplLinearArgs), _P, _Z, _P]),
     "npl_w8a8_linear_noalloc": (_I, [_P, _I, _P, _P, _I, _P, _P, _I, _I, _I, _I, _P, _I, _P, _I, _I, _P, _P]),
     "npl_store_kv": (_I, [_P, _P, _I, _I, _I, _I, _P, _P, _P, _I, _I, _P]),
     "npl_rope_store_kv": (_I, [_P, _I, _I, _I, _I, _I, _P, _P, _I, _P, _P, _P, _P, _P, _I, _I, _P]),

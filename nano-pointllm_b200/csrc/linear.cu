@@ -2,7 +2,13 @@
 //
 // Replaces w8a8.py:118-139 (integer_linear_per_output_reference) and the
 // F.linear projection call sites of the decode/prefill path (packed QKV, O,
-// packed gate/up + act_fn(gate) * up, down, LM head).
+// packed gate/up + act_fn(gate) * up, down, LM head), with the layer math
+// around them fused in:
+//   activations: int8 via TMA, or quantised in the kernel from fp16 rows,
+//                optionally RMSNorm-ed first (lightweight_runner.py:239-245)
+//   epilogues:   dequant; + residual; SiLU(gate) * up (+ per-token absmax of
+//                the result); RoPE + KV-cache store (paged_attention.py:
+//                1284-1294)
 //
 // Formulation ("swap AB"): the weight tile is the MMA's A operand and the
 // tokens are its N dimension,
@@ -11,13 +17,15 @@
 // NT = 8..64, and prefill uses NT = 128/256 token tiles.
 //
 // Per CTA (192 threads, one CTA per SM):
-//   warp 0     TMA producer: W tile [128 rows x 128 B] + X tile [NT x 128 B]
-//              per stage, 128-byte swizzle, STAGES-deep ring in shared memory
+//   warp 0     TMA producer: weight tile [128 rows x 128 B] (+ token tile
+//              [NT x 128 B] for int8 activations) per stage, 128-byte swizzle,
+//              a ring of 3-12 stages in shared memory
 //   warp 1     TMEM owner + MMA issuer (one thread): 4 MMAs of K = 32 per
 //              stage into a double-buffered int32 accumulator in TMEM
-//   warps 2-5  epilogue: tcgen05.ld (TMEM lane = weight row, column = token),
-//              dequant ((acc * sa) * sw + bias), fused residual / SiLU*up,
-//              fp16 or fp32 stores
+//   warps 2-5  before the main loop: quantise fp16 activations (with RMSNorm)
+//              into per-unit token tiles in shared memory; then the epilogue:
+//              tcgen05.ld (TMEM lane = weight row, column = token), dequant
+//              ((acc * sa) * sw + bias) and the fused tail
 //
 // Work split ("stream-K"): the (tile, k-block) units of the whole problem are
 // divided evenly over the grid. A CTA that owns a whole tile runs its
@@ -44,10 +52,19 @@ namespace {
 constexpr int kTileN = 128;   // weight rows per tile (MMA M)
 constexpr int kBlockK = 128;  // K bytes per stage (one 128-byte swizzle atom)
 constexpr int kThreads = 192;
+constexpr int kMaxStages = 12;
+constexpr int kCoresidentSmem = 110 * 1024;  // two CTAs per SM (programmatic dependent launch)
+constexpr int kMaxSmem = 226 * 1024;
 
 struct LinearArgs {
   int M, N, K;
-  const float* sa;
+  int x_mode;
+  const float* sa;         // NPL_X_INT8: per-token scales
+  const __half* xf;        // NPL_X_F16_*: fp16 activations [M, K]
+  int ldx;
+  int32_t* x_absmax;       // NPL_X_F16_ABSMAX: per-token absmax (float bits); zeroed after use
+  const __half* norm_w;    // NPL_X_F16_RMSNORM
+  float eps;
   const float* sw;
   const float* bias;
   int epilogue;
@@ -57,26 +74,41 @@ struct LinearArgs {
   int ld_out;
   int out_dtype;
   int32_t* acc_out;
-  int32_t* ws_acc;  // [grid - 1 slots][NT][128]
-  int32_t* ws_cnt;  // [grid - 1 slots]
+  int32_t* absmax_out;     // NPL_EPI_SILU_MUL: per-token max |out| (float bits), atomic max
+  const __half* cos_t;     // NPL_EPI_ROPE_KV
+  const __half* sin_t;
+  int max_position;
+  const int64_t* positions;
+  const int32_t* slots;
+  __half* q_out;
+  __half* k_cache;
+  __half* v_cache;
+  long long num_slots;
+  int heads, kv_heads, head_dim;
   int n_tiles;
   int k_blocks;
   long long total_units;
+  int stages;
+  int x_slots;
+  uint32_t off_a, off_b, off_x, off_f;
+  int32_t* ws_acc;   // [grid - 1 slots][NT][128]
+  int32_t* ws_cnt;   // [grid - 1 slots]
+  int32_t* ws_xcnt;  // [1]: CTAs done reading x_absmax
   int* status;
 };
 
-template <int NT, int STAGES>
-struct alignas(1024) LinearSmem {
-  int8_t a[STAGES][kTileN * kBlockK];
-  int8_t b[STAGES][NT * kBlockK];
-  __half xchg[8][64];  // SiLU*up: up values of one 8-column chunk
-  uint64_t full[STAGES];
-  uint64_t empty[STAGES];
+// Control block at the start of the dynamic shared memory; the stage ring,
+// the token tiles and the scale scratch follow at the offsets in LinearArgs.
+struct LinearCtl {
+  uint64_t full[kMaxStages];
+  uint64_t empty[kMaxStages];
   uint64_t tfull[2];
   uint64_t tempty[2];
   uint64_t teardown;
+  uint64_t xready;
   uint32_t tmem_base;
   int last_flag;
+  __half xchg[8][kTileN];  // epilogue exchange between TMEM lanes
 };
 
 __host__ __device__ constexpr uint32_t tmem_cols_for(int nt) {
@@ -86,6 +118,16 @@ __host__ __device__ constexpr uint32_t tmem_cols_for(int nt) {
 }
 
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ int atomic_add_acq_rel(int32_t* p, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
 
 // Iterates the CTA's stream-K segments: (tile, kb0, kb1).
 struct SegmentIter {
@@ -118,12 +160,18 @@ __device__ __forceinline__ float silu_h(float g) {
   return __half2float(__double2half(gd / (1.0 + exp(-gd))));
 }
 
+__device__ __forceinline__ void atomic_max_nonneg(int32_t* p, float v) {
+  atomicMax(p, __float_as_int(v));  // bit patterns of non-negative floats order like the values
+}
+
 // Epilogue of 8 consecutive token columns [c0, c0 + 8) of tile row `row`.
+// `sa` holds the per-token activation scales indexed by token.
 template <int NT>
-__device__ __forceinline__ void epilogue_chunk(const LinearArgs& p, __half (*xchg)[64], int m_tile, int n_tile,
-                                               int row, int c0, const int32_t (&acc)[8]) {
+__device__ __forceinline__ void epilogue_chunk(const LinearArgs& p, LinearCtl& c, const float* sa, int m_tile,
+                                               int n_tile, int row, int c0, const int32_t (&acc)[8]) {
   const int n = n_tile * kTileN + row;
   const int m_base = m_tile * NT + c0;
+  const int lane = threadIdx.x & 31;
   if (p.acc_out && n < p.N) {
 #pragma unroll
     for (int j = 0; j < 8; ++j)
@@ -136,22 +184,70 @@ __device__ __forceinline__ void epilogue_chunk(const LinearArgs& p, __half (*xch
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const int m = min(m_base + j, p.M - 1);
-        xchg[j][row - 64] = __float2half_rn(dequant(acc[j], p.sa[m], sw, p.bias, n));
+        c.xchg[j][row - 64] = __float2half_rn(dequant(acc[j], sa[m], sw, p.bias, n));
       }
     }
     epi_bar();
-    if (row < 64) {
+    if (row < 64) {  // two full warps
       const int col = n_tile * 64 + row;
       __half* out = static_cast<__half*>(p.out);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const int m = m_base + j;
+        float h = 0.f;
         if (m < p.M) {
-          const float g = __half2float(__float2half_rn(dequant(acc[j], p.sa[m], sw, p.bias, n)));
-          const float u = __half2float(xchg[j][row]);
-          out[(size_t)m * p.ld_out + col] = __float2half_rn(__fmul_rn(silu_h(g), u));
+          const float g = __half2float(__float2half_rn(dequant(acc[j], sa[m], sw, p.bias, n)));
+          const float u = __half2float(c.xchg[j][row]);
+          const __half hh = __float2half_rn(__fmul_rn(silu_h(g), u));
+          out[(size_t)m * p.ld_out + col] = hh;
+          h = fabsf(__half2float(hh));
+        }
+        if (p.absmax_out) {
+          h = warp_max(h);
+          if (lane == 0 && m < p.M) atomic_max_nonneg(p.absmax_out + m, h);
         }
       }
+    }
+    epi_bar();
+    return;
+  }
+  if (p.epilogue == NPL_EPI_ROPE_KV) {
+    // every tile lies in one of q | k | v (head blocks are multiples of 128)
+    const int D = p.head_dim, half_d = D / 2;
+    const float sw = p.sw[n];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int m = min(m_base + j, p.M - 1);
+      c.xchg[j][row] = __float2half_rn(dequant(acc[j], sa[m], sw, p.bias, n));
+    }
+    epi_bar();
+    const int q_cols = p.heads * D, k_cols = p.kv_heads * D;
+    const int d = n % D;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int m = m_base + j;
+      if (m >= p.M) break;
+      const __half x = c.xchg[j][row];
+      const long long slot = p.slots[m];
+      const bool slot_ok = slot >= 0 && slot < p.num_slots;
+      if (n >= q_cols + k_cols) {  // v
+        if (slot_ok) p.v_cache[(slot * p.kv_heads + (n - q_cols - k_cols) / D) * D + d] = x;
+        continue;
+      }
+      const long long pos = p.positions[m];
+      if (pos < 0 || pos >= p.max_position) continue;
+      const float x1 = __half2float(x);
+      const float x2 = __half2float(c.xchg[j][row ^ half_d]);
+      const float cs = __half2float(p.cos_t[pos * D + d]);
+      const float sn = __half2float(p.sin_t[pos * D + d]);
+      // rotate_half(x)[d] = -x[d + D/2] (d < D/2), x[d - D/2] (d >= D/2)
+      const float a = __half2float(__float2half_rn(__fmul_rn(x1, cs)));
+      const float b = __half2float(__float2half_rn(__fmul_rn(d < half_d ? -x2 : x2, sn)));
+      const __half o = __float2half_rn(__fadd_rn(a, b));
+      if (n < q_cols)
+        p.q_out[((size_t)m * p.heads + n / D) * D + d] = o;
+      else if (slot_ok)
+        p.k_cache[(slot * p.kv_heads + (n - q_cols) / D) * D + d] = o;
     }
     epi_bar();
     return;
@@ -162,7 +258,7 @@ __device__ __forceinline__ void epilogue_chunk(const LinearArgs& p, __half (*xch
   for (int j = 0; j < 8; ++j) {
     const int m = m_base + j;
     if (m >= p.M) break;
-    const float v = dequant(acc[j], p.sa[m], sw, p.bias, n);
+    const float v = dequant(acc[j], sa[m], sw, p.bias, n);
     if (p.epilogue == NPL_EPI_RESIDUAL) {
       const float o = __half2float(__float2half_rn(v));
       const float r = __half2float(p.residual[(size_t)m * p.ld_res + n]);
@@ -175,42 +271,218 @@ __device__ __forceinline__ void epilogue_chunk(const LinearArgs& p, __half (*xch
   }
 }
 
-template <int NT, int STAGES>
+__device__ __forceinline__ void unpack_f16x8(const uint4& x, float (&v)[8]) {
+  const __half2* h = reinterpret_cast<const __half2*>(&x);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __half22float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+
+// Activation prologue (NPL_X_F16_*), run by the 128 epilogue threads: the
+// per-token scales (and RMSNorm factors), then every token tile this CTA's
+// units need, quantised into shared memory in the MMA's 128-byte-swizzle
+// K-major layout (unit u of the CTA uses tile slot u). Same arithmetic as
+// npl_rmsnorm_quant / npl_quant_rows. Loads are issued in batches before
+// their values are used, so each batch costs one memory latency.
+constexpr int kRowGroup = 2;   // rows reduced together in the RMSNorm statistics
+constexpr int kRowChunks = 4;  // 16-byte chunks per thread and row in flight
+
+template <int NT>
+__device__ void produce_activations(const LinearArgs& p, int8_t* xslot, float* s_scale, float* s_inv, double* red,
+                                    int ct) {
+  const int ew = ct >> 5, lane = ct & 31;
+  if (p.x_mode == NPL_X_F16_RMSNORM) {
+    for (int m0 = 0; m0 < p.M; m0 += kRowGroup) {
+      double ss[kRowGroup];
+      float amax[kRowGroup];
+#pragma unroll
+      for (int r = 0; r < kRowGroup; ++r) ss[r] = 0.0;
+      // pass 1: sum of squares, each row spread over all 128 threads
+      for (int k0 = 0; k0 < p.K; k0 += 128 * 8 * kRowChunks) {
+        uint4 buf[kRowGroup][kRowChunks];
+#pragma unroll
+        for (int r = 0; r < kRowGroup; ++r)
+#pragma unroll
+          for (int j = 0; j < kRowChunks; ++j) {
+            const int k = k0 + (j * 128 + ct) * 8;
+            buf[r][j] = (m0 + r < p.M && k < p.K)
+                            ? *reinterpret_cast<const uint4*>(p.xf + (size_t)(m0 + r) * p.ldx + k)
+                            : make_uint4(0, 0, 0, 0);
+          }
+#pragma unroll
+        for (int r = 0; r < kRowGroup; ++r)
+#pragma unroll
+          for (int j = 0; j < kRowChunks; ++j) {
+            float v[8];
+            unpack_f16x8(buf[r][j], v);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) ss[r] += (double)v[i] * (double)v[i];
+          }
+      }
+#pragma unroll
+      for (int r = 0; r < kRowGroup; ++r) {
+        ss[r] = warp_sum(ss[r]);
+        if (lane == 0) red[ew * kRowGroup + r] = ss[r];
+      }
+      epi_bar();
+      float rr[kRowGroup];
+#pragma unroll
+      for (int r = 0; r < kRowGroup; ++r) {
+        const double tot = red[r] + red[kRowGroup + r] + red[2 * kRowGroup + r] + red[3 * kRowGroup + r];
+        const float mean = __double2float_rn(tot / (double)p.K);
+        rr[r] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
+        amax[r] = 0.f;
+      }
+      epi_bar();  // red is reused below
+      // pass 2 (L1-resident rows): absmax of the normalised row
+      for (int k0 = 0; k0 < p.K; k0 += 128 * 8 * kRowChunks) {
+        uint4 buf[kRowGroup][kRowChunks], wbuf[kRowChunks];
+#pragma unroll
+        for (int j = 0; j < kRowChunks; ++j) {
+          const int k = k0 + (j * 128 + ct) * 8;
+          wbuf[j] = k < p.K ? *reinterpret_cast<const uint4*>(p.norm_w + k) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+          for (int r = 0; r < kRowGroup; ++r)
+            buf[r][j] = (m0 + r < p.M && k < p.K)
+                            ? *reinterpret_cast<const uint4*>(p.xf + (size_t)(m0 + r) * p.ldx + k)
+                            : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int j = 0; j < kRowChunks; ++j) {
+          float w[8];
+          unpack_f16x8(wbuf[j], w);
+#pragma unroll
+          for (int r = 0; r < kRowGroup; ++r) {
+            float v[8];
+            unpack_f16x8(buf[r][j], v);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const float y = __half2float(__float2half_rn(__fmul_rn(v[i], rr[r])));
+              amax[r] = fmaxf(amax[r], fabsf(__half2float(__float2half_rn(__fmul_rn(w[i], y)))));
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < kRowGroup; ++r) {
+        const float a = warp_max(amax[r]);
+        if (lane == 0) red[ew * kRowGroup + r] = (double)a;
+      }
+      epi_bar();
+      if (ct < kRowGroup && m0 + ct < p.M) {
+        const float a = fmaxf(fmaxf((float)red[ct], (float)red[kRowGroup + ct]),
+                              fmaxf((float)red[2 * kRowGroup + ct], (float)red[3 * kRowGroup + ct]));
+        s_inv[m0 + ct] = rr[ct];
+        s_scale[m0 + ct] = scale_from_absmax(a);
+      }
+      epi_bar();
+    }
+  } else {
+    for (int m = ct; m < p.M; m += 128) s_scale[m] = scale_from_absmax(__int_as_float(p.x_absmax[m]));
+    epi_bar();
+  }
+  const long long u_begin = (long long)blockIdx.x * p.total_units / gridDim.x;
+  const long long u_end = (long long)(blockIdx.x + 1) * p.total_units / gridDim.x;
+  const int total = (int)(u_end - u_begin) * NT * 8;
+  const bool norm = p.x_mode == NPL_X_F16_RMSNORM;
+  constexpr int kBatch = 4;
+  for (int base_item = ct; base_item < total; base_item += 128 * kBatch) {
+    uint4 raw[kBatch][2], wraw[kBatch][2];
+#pragma unroll
+    for (int b = 0; b < kBatch; ++b) {
+      const int item = base_item + b * 128;
+      const int u = item / (NT * 8), r = (item >> 3) % NT, chunk = item & 7;
+      const int k0 = (int)((u_begin + u) % p.k_blocks) * kBlockK + chunk * 16;
+      const bool live = item < total && r < p.M && k0 < p.K;
+      const __half* src = p.xf + (size_t)r * p.ldx + k0;
+      raw[b][0] = live ? *reinterpret_cast<const uint4*>(src) : make_uint4(0, 0, 0, 0);
+      raw[b][1] = live ? *reinterpret_cast<const uint4*>(src + 8) : make_uint4(0, 0, 0, 0);
+      if (norm) {
+        wraw[b][0] = live ? *reinterpret_cast<const uint4*>(p.norm_w + k0) : make_uint4(0, 0, 0, 0);
+        wraw[b][1] = live ? *reinterpret_cast<const uint4*>(p.norm_w + k0 + 8) : make_uint4(0, 0, 0, 0);
+      }
+    }
+#pragma unroll
+    for (int b = 0; b < kBatch; ++b) {
+      const int item = base_item + b * 128;
+      if (item >= total) break;
+      const int u = item / (NT * 8), r = (item >> 3) % NT, chunk = item & 7;
+      uint4 packed = make_uint4(0, 0, 0, 0);
+      if (r < p.M) {
+        float v[16];
+        unpack_f16x8(raw[b][0], *reinterpret_cast<float(*)[8]>(v));
+        unpack_f16x8(raw[b][1], *reinterpret_cast<float(*)[8]>(v + 8));
+        if (norm) {
+          float w[16];
+          unpack_f16x8(wraw[b][0], *reinterpret_cast<float(*)[8]>(w));
+          unpack_f16x8(wraw[b][1], *reinterpret_cast<float(*)[8]>(w + 8));
+          const float rr = s_inv[r];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float y = __half2float(__float2half_rn(__fmul_rn(v[i], rr)));
+            v[i] = __half2float(__float2half_rn(__fmul_rn(w[i], y)));
+          }
+        }
+        const float sc = s_scale[r];
+        uint32_t* w32 = reinterpret_cast<uint32_t*>(&packed);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) w32[i >> 2] |= (uint32_t)(quantize_one(v[i], sc) & 0xff) << (8 * (i & 3));
+      }
+      // 128-byte swizzle: 16-byte chunk c of row r sits at chunk c ^ (r % 8)
+      *reinterpret_cast<uint4*>(xslot + (size_t)u * NT * kBlockK + r * kBlockK + ((chunk ^ (r & 7)) << 4)) = packed;
+    }
+  }
+  fence_proxy_async_smem();  // the tensor cores read these tiles through the async proxy
+}
+
+template <int NT>
 __global__ void __launch_bounds__(kThreads, 1)
     w8a8_linear_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                        const LinearArgs p) {
   extern __shared__ unsigned char smem_raw[];
-  using Smem = LinearSmem<NT, STAGES>;
-  Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                                         ~uintptr_t(1023));
+  LinearCtl& c = *reinterpret_cast<LinearCtl*>(base);
+  int8_t* ring_a = reinterpret_cast<int8_t*>(base + p.off_a);
+  int8_t* ring_b = reinterpret_cast<int8_t*>(base + p.off_b);
+  int8_t* xslot = reinterpret_cast<int8_t*>(base + p.off_x);
+  float* s_scale = reinterpret_cast<float*>(base + p.off_f);
+  float* s_inv = s_scale + NT;
   constexpr uint32_t kTmemCols = tmem_cols_for(NT);
-  constexpr uint32_t kStageBytes = kTileN * kBlockK + NT * kBlockK;
   constexpr uint32_t kIdesc = idesc_i8(kTileN, NT);
+  const bool x_int8 = p.x_mode == NPL_X_INT8;
+  const uint32_t stage_bytes = kTileN * kBlockK + (x_int8 ? NT * kBlockK : 0);
+  const int stages = p.stages;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
     prefetch_tensormap(&tmap_w);
-    prefetch_tensormap(&tmap_x);
-    for (int i = 0; i < STAGES; ++i) {
-      mbar_init(&s.full[i], 1);
-      mbar_init(&s.empty[i], 1);
+    if (x_int8) prefetch_tensormap(&tmap_x);
+    for (int i = 0; i < stages; ++i) {
+      mbar_init(&c.full[i], 1);
+      mbar_init(&c.empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&s.tfull[i], 1);
-      mbar_init(&s.tempty[i], 4);
+      mbar_init(&c.tfull[i], 1);
+      mbar_init(&c.tempty[i], 4);
     }
-    mbar_init(&s.teardown, 1);
+    mbar_init(&c.teardown, 1);
+    mbar_init(&c.xready, 128);
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(&s.tmem_base, kTmemCols);
+    tmem_alloc(&c.tmem_base, kTmemCols);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem_base = s.tmem_base;
+  const uint32_t tmem_base = c.tmem_base;
   pdl_trigger();  // the next kernel may start launching its CTAs
 
   if (warp == 0) {
@@ -225,15 +497,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       {
         SegmentIter it(p);
         int tile, kb0, kb1;
-        while (pre < STAGES && it.next(tile, kb0, kb1)) {
+        while (pre < stages && it.next(tile, kb0, kb1)) {
           const int n_tile = tile % p.n_tiles;
-          for (int kb = kb0; kb < kb1 && pre < STAGES; ++kb, ++pre) {
-            mbar_arrive_expect_tx(&s.full[pre], kStageBytes);
-            tma_load_2d(s.a[pre], &tmap_w, kb * kBlockK, n_tile * kTileN, &s.full[pre], pol_w);
+          for (int kb = kb0; kb < kb1 && pre < stages; ++kb, ++pre) {
+            mbar_arrive_expect_tx(&c.full[pre], stage_bytes);
+            tma_load_2d(ring_a + (size_t)pre * kTileN * kBlockK, &tmap_w, kb * kBlockK, n_tile * kTileN,
+                        &c.full[pre], pol_w);
           }
         }
       }
-      uint32_t outstanding = pre >= 32 ? 0xffffffffu : ((1u << pre) - 1);  // stages holding a load
+      uint32_t outstanding = (1u << pre) - 1;  // stages holding a load (pre <= 12)
       pdl_wait();
       SegmentIter it(p);
       int tile, kb0, kb1, stage = 0, unit = 0;
@@ -243,84 +516,100 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int m_tile = tile / p.n_tiles, n_tile = tile % p.n_tiles;
         for (int kb = kb0; kb < kb1; ++kb, ++unit) {
           if (unit >= pre) {
-            if (!mbar_wait(&s.empty[stage], phase ^ 1, p.status, NPL_DEV_TIMEOUT_TMA)) {
+            if (!mbar_wait(&c.empty[stage], phase ^ 1, p.status, NPL_DEV_TIMEOUT_TMA)) {
               ok = false;
               break;
             }
-            mbar_arrive_expect_tx(&s.full[stage], kStageBytes);
-            tma_load_2d(s.a[stage], &tmap_w, kb * kBlockK, n_tile * kTileN, &s.full[stage], pol_w);
+            mbar_arrive_expect_tx(&c.full[stage], stage_bytes);
+            tma_load_2d(ring_a + (size_t)stage * kTileN * kBlockK, &tmap_w, kb * kBlockK, n_tile * kTileN,
+                        &c.full[stage], pol_w);
           }
-          tma_load_2d(s.b[stage], &tmap_x, kb * kBlockK, m_tile * NT, &s.full[stage], pol_x);
+          if (x_int8)
+            tma_load_2d(ring_b + (size_t)stage * NT * kBlockK, &tmap_x, kb * kBlockK, m_tile * NT, &c.full[stage],
+                        pol_x);
           outstanding |= 1u << stage;
-          if (++stage == STAGES) {
+          if (++stage == stages) {
             stage = 0;
             phase ^= 1;
           }
         }
       }
-
       // Drain: every issued load must land before the CTA's shared memory is
       // released. A stage's last load used parity (phase of that issue).
-      for (int i = 0; i < STAGES; ++i) {
+      for (int i = 0; i < stages; ++i) {
         if (!(outstanding >> i & 1)) continue;
-        // stages before `stage` were last issued in the current phase, the
-        // others in the previous one
         const uint32_t par = i < stage ? phase : phase ^ 1;
-        mbar_wait(&s.full[i], par, p.status, NPL_DEV_TIMEOUT_TEARDOWN);
+        mbar_wait(&c.full[i], par, p.status, NPL_DEV_TIMEOUT_TEARDOWN);
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
+      bool ok = x_int8 || mbar_wait(&c.xready, 0, p.status, NPL_DEV_TIMEOUT_MMA);
       SegmentIter it(p);
-      int tile, kb0, kb1, stage = 0, seg = 0;
+      int tile, kb0, kb1, stage = 0, seg = 0, unit = 0;
       uint32_t phase = 0;
-      bool ok = true;
       while (ok && it.next(tile, kb0, kb1)) {
         const int buf = seg & 1;
         const uint32_t tphase = (seg >> 1) & 1;
-        if (!mbar_wait(&s.tempty[buf], tphase ^ 1, p.status, NPL_DEV_TIMEOUT_MMA)) break;
+        if (!mbar_wait(&c.tempty[buf], tphase ^ 1, p.status, NPL_DEV_TIMEOUT_MMA)) break;
         tc_fence_after();
         const uint32_t d = tmem_base + (uint32_t)(buf * NT);
-        for (int kb = kb0; kb < kb1; ++kb) {
-          if (!mbar_wait(&s.full[stage], phase, p.status, NPL_DEV_TIMEOUT_MMA)) {
+        for (int kb = kb0; kb < kb1; ++kb, ++unit) {
+          if (!mbar_wait(&c.full[stage], phase, p.status, NPL_DEV_TIMEOUT_MMA)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a0 = smem_u32(s.a[stage]);
-          const uint32_t b0 = smem_u32(s.b[stage]);
+          const uint32_t a0 = smem_u32(ring_a + (size_t)stage * kTileN * kBlockK);
+          const uint32_t b0 = x_int8 ? smem_u32(ring_b + (size_t)stage * NT * kBlockK)
+                                     : smem_u32(xslot + (size_t)unit * NT * kBlockK);
 #pragma unroll
           for (int kk = 0; kk < kBlockK / 32; ++kk) {
             mma_i8(d, sdesc_k_sw128(a0 + kk * 32), sdesc_k_sw128(b0 + kk * 32), kIdesc,
                    (kb > kb0 || kk > 0) ? 1u : 0u);
           }
-          tc_commit(&s.empty[stage]);
-          if (++stage == STAGES) {
+          tc_commit(&c.empty[stage]);
+          if (++stage == stages) {
             stage = 0;
             phase ^= 1;
           }
         }
         if (!ok) break;
-        tc_commit(&s.tfull[buf]);
+        tc_commit(&c.tfull[buf]);
         ++seg;
       }
       // all MMAs issued by this thread complete before TMEM is freed
-      tc_commit(&s.teardown);
-      mbar_wait(&s.teardown, 0, p.status, NPL_DEV_TIMEOUT_TEARDOWN);
+      tc_commit(&c.teardown);
+      mbar_wait(&c.teardown, 0, p.status, NPL_DEV_TIMEOUT_TEARDOWN);
     }
   } else {
     // -------------------------------------------------------------- epilogue
     const int quarter = warp & 3;  // TMEM lanes this warp may access
     const int row = quarter * 32 + lane;
+    const int ct = threadIdx.x - 64;
     pdl_wait();
+    if (!x_int8) {
+      produce_activations<NT>(p, xslot, s_scale, s_inv, reinterpret_cast<double*>(s_inv + NT), ct);
+      mbar_arrive(&c.xready);
+      if (p.x_mode == NPL_X_F16_ABSMAX) {
+        // x_absmax is consumed: the last CTA to have read it zeroes it for the
+        // producer of the next call
+        epi_bar();
+        if (ct == 0 && atomic_add_acq_rel(p.ws_xcnt, 1) + 1 == (int)gridDim.x) {
+          for (int m = 0; m < p.M; ++m) p.x_absmax[m] = 0;
+          *p.ws_xcnt = 0;
+        }
+      }
+    }
+    const float* sa = x_int8 ? p.sa : s_scale;
     SegmentIter it(p);
     int tile, kb0, kb1, seg = 0;
     while (it.next(tile, kb0, kb1)) {
       const int buf = seg & 1;
       const uint32_t tphase = (seg >> 1) & 1;
       const int m_tile = tile / p.n_tiles, n_tile = tile % p.n_tiles;
-      if (!mbar_wait(&s.tfull[buf], tphase, p.status, NPL_DEV_TIMEOUT_EPILOGUE)) break;
+      if (!mbar_wait(&c.tfull[buf], tphase, p.status, NPL_DEV_TIMEOUT_EPILOGUE)) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(buf * NT);
       const bool whole = (kb0 == 0 && kb1 == p.k_blocks);
@@ -333,7 +622,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           int32_t acc[8];
           tmem_ld_x8(taddr + c0, acc);
           tmem_wait_ld();
-          epilogue_chunk<NT>(p, s.xchg, m_tile, n_tile, row, c0, acc);
+          epilogue_chunk<NT>(p, c, sa, m_tile, n_tile, row, c0, acc);
         }
       } else {
         for (int c0 = 0; c0 < NT; c0 += 8) {
@@ -348,17 +637,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       // accumulator buffer free for the next segment's MMAs
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&s.tempty[buf]);
+      if (lane == 0) mbar_arrive(&c.tempty[buf]);
       if (!whole) {
-        __threadfence();
         epi_bar();
-        if (threadIdx.x == 64) {
-          const int prev = atomicAdd(p.ws_cnt + slot, kb1 - kb0);
-          s.last_flag = (prev + (kb1 - kb0) == p.k_blocks);
-        }
+        if (ct == 0) c.last_flag = (atomic_add_acq_rel(p.ws_cnt + slot, kb1 - kb0) + (kb1 - kb0) == p.k_blocks);
         epi_bar();
-        if (s.last_flag) {
-          __threadfence();
+        if (c.last_flag) {
           for (int c0 = 0; c0 < NT; c0 += 8) {
             int32_t acc[8];
 #pragma unroll
@@ -367,9 +651,9 @@ __global__ void __launch_bounds__(kThreads, 1)
               acc[j] = __ldcg(cell);
               __stcg(cell, 0);
             }
-            epilogue_chunk<NT>(p, s.xchg, m_tile, n_tile, row, c0, acc);
+            epilogue_chunk<NT>(p, c, sa, m_tile, n_tile, row, c0, acc);
           }
-          if (threadIdx.x == 64) p.ws_cnt[slot] = 0;
+          if (ct == 0) p.ws_cnt[slot] = 0;
         }
         epi_bar();
       }
@@ -422,8 +706,9 @@ int pick_nt(int M) {
   return 256;
 }
 
-// Workspace: grid - 1 partial-tile slots of NT x 128 int32 plus one counter
-// per slot; grid <= number of SMs of the current device.
+// Workspace: grid - 1 partial-tile slots of NT x 128 int32, one counter per
+// slot and one activation-reader counter; grid <= number of SMs of the
+// current device.
 int max_grid() {
   const int sms = num_sms();
   return sms > 0 ? sms : 148;
@@ -436,21 +721,179 @@ size_t ws_acc_bytes(int M) {
 
 size_t ws_bytes(int M) {
   const size_t slots = (size_t)std::max(1, max_grid() - 1);
-  return ws_acc_bytes(M) + ((slots * sizeof(int32_t) + 255) & ~size_t(255));
+  return ws_acc_bytes(M) + (((slots + 1) * sizeof(int32_t) + 255) & ~size_t(255));
 }
 
-template <int NT, int STAGES>
-int launch_linear(const CUtensorMap& tw, const CUtensorMap& tx, LinearArgs& p, cudaStream_t st) {
-  auto kern = w8a8_linear_kernel<NT, STAGES>;
-  const int smem = (int)sizeof(LinearSmem<NT, STAGES>) + 1024;
-  static bool configured = false;  // per instantiation; attribute is per device function
-  if (!configured) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
-      return launch_status("npl_w8a8_linear: smem attribute");
-    configured = true;
-  }
-  const long long grid = std::min<long long>(max_grid(), p.total_units);
+constexpr uint32_t align1k(size_t x) { return (uint32_t)((x + 1023) & ~size_t(1023)); }
+
+template <int NT>
+int launch_linear(const CUtensorMap& tw, const CUtensorMap& tx, LinearArgs& p, int grid, cudaStream_t st) {
+  auto kern = w8a8_linear_kernel<NT>;
+  const bool x_int8 = p.x_mode == NPL_X_INT8;
+  const size_t stage_bytes = (size_t)kTileN * kBlockK + (x_int8 ? (size_t)NT * kBlockK : 0);
+  const size_t xslots = x_int8 ? 0 : (size_t)p.x_slots * NT * kBlockK;
+  p.off_a = align1k(sizeof(LinearCtl));
+  // Decode tiles (NT <= 64) keep the CTA near 110 KB when they can, so that
+  // the next kernel's CTA fits beside it on an SM and starts its weight loads
+  // while this one finishes; prefill tiles take the whole shared memory.
+  const size_t fixed = p.off_a + xslots + 2 * NT * sizeof(float) + 8 * sizeof(double) + 1024 + 1024;
+  int stages = 0;
+  if (NT <= 64 && fixed + 3 * stage_bytes <= (size_t)kCoresidentSmem)
+    stages = (int)std::min<size_t>(6, (kCoresidentSmem - fixed) / stage_bytes);
+  else if (fixed + 2 * stage_bytes <= (size_t)kMaxSmem)
+    stages = (int)std::min<size_t>(kMaxStages, (kMaxSmem - fixed) / stage_bytes);
+  if (stages < 2)
+    return fail(NPL_ERR_UNSUPPORTED, "npl_w8a8_linear: %d fp16 token tiles do not fit in shared memory", p.x_slots);
+  p.stages = stages;
+  p.off_b = p.off_a + (uint32_t)(stages * kTileN * kBlockK);
+  p.off_x = p.off_b + (uint32_t)(x_int8 ? stages * NT * kBlockK : 0);
+  p.off_f = p.off_x + (uint32_t)xslots;
+  const int smem = (int)(p.off_f + 2 * NT * sizeof(float) + 8 * sizeof(double) + 1024);
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    return launch_status("npl_w8a8_linear: smem attribute");
   return launch_pdl("npl_w8a8_linear", kern, dim3((unsigned)grid), dim3(kThreads), (size_t)smem, st, tw, tx, p);
+}
+
+struct LinearCall {
+  const int8_t* qa;
+  int lda;
+  const float* sa;
+  const void* xf;
+  int ldx;
+  int32_t* x_absmax;
+  const void* norm_w;
+  float eps;
+  int x_mode;
+  const int8_t* qw;
+  int ldw;
+  const float* sw;
+  const float* bias;
+  int M, N, K;
+  int epilogue;
+  const void* residual;
+  int ld_res;
+  void* out;
+  int ld_out;
+  int out_dtype;
+  int32_t* acc_out;
+  int32_t* absmax_out;
+  const npl_rope_kv* rope;
+};
+
+int run_linear(const LinearCall& a, void* workspace, size_t workspace_bytes, void* stream) {
+  if (int rc = check_device()) return rc;
+  const int M = a.M, N = a.N, K = a.K;
+  if (!a.qw || !a.sw) return fail(NPL_ERR_ARG, "npl_w8a8_linear: null weight or weight scales");
+  if (M < 0 || N <= 0 || K <= 0 || K % 16 || a.ldw < K || a.ldw % 16)
+    return fail(NPL_ERR_ARG, "npl_w8a8_linear: bad shape M=%d N=%d K=%d ldw=%d", M, N, K, a.ldw);
+  if ((long long)K * 127 * 127 >= (1ll << 31))
+    return fail(NPL_ERR_OVERFLOW, "npl_w8a8_linear: worst-case dot product exceeds signed INT32 (K=%d)", K);
+  if (!aligned16(a.qw)) return fail(NPL_ERR_ARG, "npl_w8a8_linear: int8 weights must be 16-byte aligned");
+  if (a.x_mode == NPL_X_INT8) {
+    if (!a.qa || !a.sa || a.lda < K || a.lda % 16 || !aligned16(a.qa))
+      return fail(NPL_ERR_ARG, "npl_w8a8_linear: int8 activations need qa/sa, lda >= K, lda %% 16 == 0, 16-B alignment");
+  } else if (a.x_mode == NPL_X_F16_ABSMAX || a.x_mode == NPL_X_F16_RMSNORM) {
+    if (!a.xf || a.ldx < K || a.ldx % 8 || !aligned16(a.xf))
+      return fail(NPL_ERR_ARG, "npl_w8a8_linear: fp16 activations need x, ldx >= K, ldx %% 8 == 0, 16-B alignment");
+    if (M > 64) return fail(NPL_ERR_UNSUPPORTED, "npl_w8a8_linear: fp16 activations take at most 64 tokens");
+    if (a.x_mode == NPL_X_F16_ABSMAX && !a.x_absmax)
+      return fail(NPL_ERR_ARG, "npl_w8a8_linear: NPL_X_F16_ABSMAX needs the per-token absmax");
+    if (a.x_mode == NPL_X_F16_RMSNORM && (!a.norm_w || !aligned16(a.norm_w)))
+      return fail(NPL_ERR_ARG, "npl_w8a8_linear: NPL_X_F16_RMSNORM needs a 16-B aligned norm weight");
+  } else {
+    return fail(NPL_ERR_ARG, "npl_w8a8_linear: unknown activation mode %d", a.x_mode);
+  }
+  if (a.epilogue == NPL_EPI_RESIDUAL) {
+    if (!a.out || !a.residual || a.out_dtype != NPL_F16 || a.ld_res < N || a.ld_out < N)
+      return fail(NPL_ERR_ARG, "npl_w8a8_linear: residual epilogue needs fp16 residual/out with ld >= N");
+  } else if (a.epilogue == NPL_EPI_SILU_MUL) {
+    if (!a.out || N % kTileN || a.out_dtype != NPL_F16 || a.ld_out < N / 2)
+      return fail(NPL_ERR_ARG, "npl_w8a8_linear: SiLU*up epilogue needs N %% 128 == 0, fp16 out, ld_out >= N/2");
+  } else if (a.epilogue == NPL_EPI_NONE) {
+    if (!a.out || (a.out_dtype != NPL_F16 && a.out_dtype != NPL_F32) || a.ld_out < N)
+      return fail(NPL_ERR_ARG, "npl_w8a8_linear: out_dtype must be NPL_F16/NPL_F32 and ld_out >= N");
+  } else if (a.epilogue == NPL_EPI_ROPE_KV) {
+    const npl_rope_kv* r = a.rope;
+    if (!r || !r->cos_table || !r->sin_table || !r->positions || !r->slot_mapping || !r->q_out || !r->k_cache ||
+        !r->v_cache)
+      return fail(NPL_ERR_ARG, "npl_w8a8_linear: RoPE epilogue needs tables, positions, slots, q_out and caches");
+    const int D = r->head_dim;
+    if (D <= 0 || D % 2 || kTileN % D || (r->heads * D) % kTileN || (r->kv_heads * D) % kTileN ||
+        r->heads % r->kv_heads || N != (r->heads + 2 * r->kv_heads) * D || r->max_position <= 0 ||
+        r->num_blocks <= 0 || r->block_size <= 0)
+      return fail(NPL_ERR_ARG, "npl_w8a8_linear: RoPE epilogue geometry (N = (H + 2 Hkv) D, head blocks of 128)");
+  } else {
+    return fail(NPL_ERR_ARG, "npl_w8a8_linear: unknown epilogue %d", a.epilogue);
+  }
+  if (M == 0) return NPL_OK;
+  const size_t need = ws_bytes(M);
+  if (!workspace || workspace_bytes < need || !aligned16(workspace))
+    return fail(NPL_ERR_ARG, "npl_w8a8_linear: workspace of %zu bytes (16-byte aligned) required", need);
+
+  const int nt = pick_nt(M);
+  LinearArgs p{};
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.x_mode = a.x_mode;
+  p.sa = a.sa;
+  p.xf = static_cast<const __half*>(a.xf);
+  p.ldx = a.ldx;
+  p.x_absmax = a.x_absmax;
+  p.norm_w = static_cast<const __half*>(a.norm_w);
+  p.eps = a.eps;
+  p.sw = a.sw;
+  p.bias = a.bias;
+  p.epilogue = a.epilogue;
+  p.residual = static_cast<const __half*>(a.residual);
+  p.ld_res = a.ld_res;
+  p.out = a.out;
+  p.ld_out = a.ld_out;
+  p.out_dtype = a.out_dtype;
+  p.acc_out = a.acc_out;
+  p.absmax_out = a.absmax_out;
+  if (a.epilogue == NPL_EPI_ROPE_KV) {
+    const npl_rope_kv* r = a.rope;
+    p.cos_t = static_cast<const __half*>(r->cos_table);
+    p.sin_t = static_cast<const __half*>(r->sin_table);
+    p.max_position = r->max_position;
+    p.positions = r->positions;
+    p.slots = r->slot_mapping;
+    p.q_out = static_cast<__half*>(r->q_out);
+    p.k_cache = static_cast<__half*>(r->k_cache);
+    p.v_cache = static_cast<__half*>(r->v_cache);
+    p.num_slots = (long long)r->num_blocks * r->block_size;
+    p.heads = r->heads;
+    p.kv_heads = r->kv_heads;
+    p.head_dim = r->head_dim;
+  }
+  p.ws_acc = static_cast<int32_t*>(workspace);
+  p.ws_cnt = reinterpret_cast<int32_t*>(static_cast<char*>(workspace) + ws_acc_bytes(M));
+  p.ws_xcnt = p.ws_cnt + std::max(1, max_grid() - 1);
+  p.n_tiles = (N + kTileN - 1) / kTileN;
+  p.k_blocks = (K + kBlockK - 1) / kBlockK;
+  const int m_tiles = (M + nt - 1) / nt;
+  p.total_units = (long long)p.n_tiles * m_tiles * p.k_blocks;
+  p.status = device_status_ptr();
+  const int grid = (int)std::min<long long>(max_grid(), p.total_units);
+  p.x_slots = (int)((p.total_units + grid - 1) / grid);
+
+  CUtensorMap tw, tx;
+  if (int rc = make_map(&tw, a.qw, N, K, a.ldw, kTileN)) return rc;
+  if (a.x_mode == NPL_X_INT8) {
+    if (int rc = make_map(&tx, a.qa, M, K, a.lda, nt)) return rc;
+  } else {
+    tx = tw;  // unused
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch (nt) {
+    case 8: return launch_linear<8>(tw, tx, p, grid, st);
+    case 16: return launch_linear<16>(tw, tx, p, grid, st);
+    case 32: return launch_linear<32>(tw, tx, p, grid, st);
+    case 64: return launch_linear<64>(tw, tx, p, grid, st);
+    case 128: return launch_linear<128>(tw, tx, p, grid, st);
+    default: return launch_linear<256>(tw, tx, p, grid, st);
+  }
 }
 
 }  // namespace
@@ -468,69 +911,64 @@ extern "C" int npl_w8a8_linear(const int8_t* qa, int lda, const float* sa, const
                                const float* sw, const float* bias, int M, int N, int K, int epilogue,
                                const void* residual, int ld_res, void* out, int ld_out, int out_dtype,
                                int32_t* acc_out, void* workspace, size_t workspace_bytes, void* stream) {
-  if (int rc = check_device()) return rc;
-  if (!qa || !sa || !qw || !sw || !out) return fail(NPL_ERR_ARG, "npl_w8a8_linear: null pointer");
-  if (M < 0 || N <= 0 || K <= 0 || K % 16 || lda < K || lda % 16 || ldw < K || ldw % 16)
-    return fail(NPL_ERR_ARG, "npl_w8a8_linear: bad shape M=%d N=%d K=%d lda=%d ldw=%d", M, N, K, lda, ldw);
-  if ((long long)K * 127 * 127 >= (1ll << 31))
-    return fail(NPL_ERR_OVERFLOW, "npl_w8a8_linear: worst-case dot product exceeds signed INT32 (K=%d)", K);
-  if (!aligned16(qa) || !aligned16(qw)) return fail(NPL_ERR_ARG, "npl_w8a8_linear: int8 operands must be 16-byte aligned");
-  if (epilogue == NPL_EPI_RESIDUAL) {
-    if (!residual || out_dtype != NPL_F16 || ld_res < N || ld_out < N)
-      return fail(NPL_ERR_ARG, "npl_w8a8_linear: residual epilogue needs fp16 residual/out with ld >= N");
-  } else if (epilogue == NPL_EPI_SILU_MUL) {
-    if (N % kTileN || out_dtype != NPL_F16 || ld_out < N / 2)
-      return fail(NPL_ERR_ARG, "npl_w8a8_linear: SiLU*up epilogue needs N %% 128 == 0, fp16 out, ld_out >= N/2");
-  } else if (epilogue == NPL_EPI_NONE) {
-    if ((out_dtype != NPL_F16 && out_dtype != NPL_F32) || ld_out < N)
-      return fail(NPL_ERR_ARG, "npl_w8a8_linear: out_dtype must be NPL_F16/NPL_F32 and ld_out >= N");
-  } else {
-    return fail(NPL_ERR_ARG, "npl_w8a8_linear: unknown epilogue %d", epilogue);
-  }
-  if (M == 0) return NPL_OK;
-  const size_t need = ws_bytes(M);
-  if (!workspace || workspace_bytes < need || !aligned16(workspace))
-    return fail(NPL_ERR_ARG, "npl_w8a8_linear: workspace of %zu bytes (16-byte aligned) required", need);
-
-  const int nt = pick_nt(M);
-  LinearArgs p{};
-  p.M = M;
-  p.N = N;
-  p.K = K;
-  p.sa = sa;
-  p.sw = sw;
-  p.bias = bias;
-  p.epilogue = epilogue;
-  p.residual = static_cast<const __half*>(residual);
-  p.ld_res = ld_res;
-  p.out = out;
-  p.ld_out = ld_out;
-  p.out_dtype = out_dtype;
-  p.acc_out = acc_out;
-  p.ws_acc = static_cast<int32_t*>(workspace);
-  p.ws_cnt = reinterpret_cast<int32_t*>(static_cast<char*>(workspace) + ws_acc_bytes(M));
-  p.n_tiles = (N + kTileN - 1) / kTileN;
-  p.k_blocks = (K + kBlockK - 1) / kBlockK;
-  const int m_tiles = (M + nt - 1) / nt;
-  p.total_units = (long long)p.n_tiles * m_tiles * p.k_blocks;
-  p.status = device_status_ptr();
-
-  CUtensorMap tw, tx;
-  if (int rc = make_map(&tw, qw, N, K, ldw, kTileN)) return rc;
-  if (int rc = make_map(&tx, qa, M, K, lda, nt)) return rc;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  // Decode tiles (NT <= 64) keep the ring near 100 KB so that the next
-  // kernel's CTA fits beside this one on an SM and starts its weight loads
-  // while this one finishes (programmatic dependent launch).
-  switch (nt) {
-    case 8: return launch_linear<8, 6>(tw, tx, p, st);
-    case 16: return launch_linear<16, 6>(tw, tx, p, st);
-    case 32: return launch_linear<32, 5>(tw, tx, p, st);
-    case 64: return launch_linear<64, 4>(tw, tx, p, st);
-    case 128: return launch_linear<128, 6>(tw, tx, p, st);
-    default: return launch_linear<256, 4>(tw, tx, p, st);
-  }
+  if (epilogue != NPL_EPI_NONE && epilogue != NPL_EPI_RESIDUAL && epilogue != NPL_EPI_SILU_MUL)
+    return fail(NPL_ERR_ARG, "npl_w8a8_linear: epilogue %d (NONE, RESIDUAL or SILU_MUL; see npl_w8a8_linear_ex)",
+                epilogue);
+  if (!qa || !sa || !out) return fail(NPL_ERR_ARG, "npl_w8a8_linear: null pointer");
+  LinearCall a{};
+  a.qa = qa;
+  a.lda = lda;
+  a.sa = sa;
+  a.x_mode = NPL_X_INT8;
+  a.qw = qw;
+  a.ldw = ldw;
+  a.sw = sw;
+  a.bias = bias;
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.epilogue = epilogue;
+  a.residual = residual;
+  a.ld_res = ld_res;
+  a.out = out;
+  a.ld_out = ld_out;
+  a.out_dtype = out_dtype;
+  a.acc_out = acc_out;
+  return run_linear(a, workspace, workspace_bytes, stream);
 }
+
+extern "C" int npl_w8a8_linear_ex(const npl_linear_args* args, void* workspace, size_t workspace_bytes,
+                                  void* stream) {
+  if (!args) return fail(NPL_ERR_ARG, "npl_w8a8_linear_ex: null args");
+  LinearCall a{};
+  a.qa = args->qa;
+  a.lda = args->lda;
+  a.sa = args->sa;
+  a.xf = args->x_f16;
+  a.ldx = args->ldx;
+  a.x_absmax = args->x_absmax;
+  a.norm_w = args->norm_weight;
+  a.eps = args->eps;
+  a.x_mode = args->x_mode;
+  a.qw = args->qw;
+  a.ldw = args->ldw;
+  a.sw = args->sw;
+  a.bias = args->bias;
+  a.M = args->M;
+  a.N = args->N;
+  a.K = args->K;
+  a.epilogue = args->epilogue;
+  a.residual = args->residual;
+  a.ld_res = args->ld_res;
+  a.out = args->out;
+  a.ld_out = args->ld_out;
+  a.out_dtype = args->out_dtype;
+  a.acc_out = args->acc_out;
+  a.absmax_out = args->absmax_out;
+  a.rope = &args->rope;
+  return run_linear(a, workspace, workspace_bytes, stream);
+}
+
 
 // ----------------------------------------------------------------------------
 // npl_w8a8_linear_noalloc: the same linear for callers that cannot allocate.

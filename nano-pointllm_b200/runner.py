@@ -15,12 +15,19 @@ Reference structure followed (nanopointllm):
 
 Every Linear (packed QKV, O, packed gate/up, down, LM head) is W8A8: int8
 weights quantised once per output channel, int8 activations quantised per
-token, int32 accumulation on the tensor cores, dequant fused into the linear's
-epilogue together with the residual add (O, down) and SiLU(gate) * up. The
-decode step per layer is 9 kernels of libnpl_w8a8 and nothing else:
+token, int32 accumulation on the tensor cores. A decode step runs nine
+kernels of libnpl_w8a8 per layer and nothing else:
 
-  rmsnorm+quant -> QKV -> RoPE+store -> paged attention(+quant) ->
-  O(+residual) -> rmsnorm+quant -> gate/up(+SiLU*up) -> quant -> down(+residual)
+  RMSNorm+quant -> QKV -> RoPE + KV store -> paged attention [+quant] ->
+  O [+residual] -> RMSNorm+quant -> gate/up [SiLU*up] -> quant ->
+  down [+residual]
+
+(brackets: fused into that kernel). Every kernel launches with programmatic
+dependent launch, so the small normalisation / quantisation / RoPE kernels
+overlap the launch and weight prefetch of the next linear. (Folding them into
+the linears themselves -- the fp16-activation and RoPE modes of
+npl_w8a8_linear_ex -- measured slower on B200: it lengthens the linear's
+critical path by more than the small kernel costs.)
 
 Prefill attention over multi-token rows uses torch SDPA per sequence on the
 pool (the reference runs its own Triton varlen kernel there); the prefill

@@ -8,6 +8,7 @@ must be CUDA tensors (there is no CPU path).
 """
 from __future__ import annotations
 
+import ctypes
 from dataclasses import asdict, dataclass
 from typing import Any
 
@@ -104,6 +105,57 @@ def linear_q(qa: torch.Tensor, sa: torch.Tensor, qweight: torch.Tensor, wscale: 
         qa.data_ptr(), qa.stride(0), sa.data_ptr(), qweight.data_ptr(), qweight.stride(0), wscale.data_ptr(),
         L.ptr(bias), m, n, k, epilogue, L.ptr(res), 0 if res is None else res.stride(0), out.data_ptr(),
         out.stride(0), _DT[out.dtype], L.ptr(acc_out), ws.data_ptr(), ws.numel(), L.stream_ptr(qa.device)))
+    return out
+
+
+def linear_ex(qweight: torch.Tensor, wscale: torch.Tensor, *, x_mode: int, m: int,
+              qa: torch.Tensor | None = None, sa: torch.Tensor | None = None,
+              x_f16: torch.Tensor | None = None, x_absmax: torch.Tensor | None = None,
+              norm_weight: torch.Tensor | None = None, eps: float = 1e-6, bias: torch.Tensor | None = None,
+              epilogue: int = L.EPI_NONE, residual: torch.Tensor | None = None, out: torch.Tensor | None = None,
+              out_dtype: torch.dtype = torch.float16, acc_out: torch.Tensor | None = None,
+              absmax_out: torch.Tensor | None = None, rope: dict | None = None) -> torch.Tensor | None:
+    """npl_w8a8_linear_ex: the decode linear with its activation preparation
+    (int8 / fp16 + given absmax / fp16 + RMSNorm) and epilogue (dequant,
+    residual, SiLU*up (+ absmax), RoPE + KV store) in one kernel.
+
+    ``rope`` (for EPI_ROPE_KV): dict with cos, sin, positions, slots, q_out,
+    k_cache, v_cache, heads, kv_heads, head_dim. Returns ``out`` (None for
+    EPI_ROPE_KV, whose outputs are rope["q_out"] and the caches).
+    """
+    n, k = qweight.shape
+    dev = qweight.device
+    if epilogue != L.EPI_ROPE_KV and out is None:
+        cols = n // 2 if epilogue == L.EPI_SILU_MUL else n
+        out = torch.empty((m, cols), dtype=torch.float16 if epilogue else out_dtype, device=dev)
+    a = L.NplLinearArgs()
+    a.x_mode = x_mode
+    if x_mode == L.X_INT8:
+        a.qa, a.lda, a.sa = qa.data_ptr(), qa.stride(0), sa.data_ptr()
+    else:
+        a.x_f16, a.ldx = x_f16.data_ptr(), x_f16.stride(0)
+        a.x_absmax = L.ptr(x_absmax)
+        a.norm_weight = L.ptr(norm_weight)
+        a.eps = float(eps)
+    a.qw, a.ldw, a.sw, a.bias = qweight.data_ptr(), qweight.stride(0), wscale.data_ptr(), L.ptr(bias)
+    a.M, a.N, a.K = m, n, k
+    a.epilogue = epilogue
+    if residual is not None:
+        a.residual, a.ld_res = residual.data_ptr(), residual.stride(0)
+    if out is not None:
+        a.out, a.ld_out, a.out_dtype = out.data_ptr(), out.stride(0), _DT[out.dtype]
+    a.acc_out = L.ptr(acc_out)
+    a.absmax_out = L.ptr(absmax_out)
+    if rope is not None:
+        r = a.rope
+        r.cos_table, r.sin_table = rope["cos"].data_ptr(), rope["sin"].data_ptr()
+        r.max_position = rope["cos"].shape[0]
+        r.positions, r.slot_mapping = rope["positions"].data_ptr(), rope["slots"].data_ptr()
+        r.q_out, r.k_cache, r.v_cache = rope["q_out"].data_ptr(), rope["k_cache"].data_ptr(), rope["v_cache"].data_ptr()
+        r.num_blocks, r.block_size = rope["k_cache"].shape[0], rope["k_cache"].shape[1]
+        r.heads, r.kv_heads, r.head_dim = rope["heads"], rope["kv_heads"], rope["head_dim"]
+    ws = linear_workspace(dev, m, n, k)
+    L.check(L.lib.npl_w8a8_linear_ex(ctypes.byref(a), ws.data_ptr(), ws.numel(), L.stream_ptr(dev)))
     return out
 
 

@@ -47,3 +47,23 @@ def test_workspace_sizes_are_host_only():
     assert n >= 8 * 128 * 4
     a = _lib.lib.npl_decode_attention_workspace_bytes(8, 32, 128, 5, 256)
     assert a >= 8 * 32 * 5 * (128 + 2) * 4
+
+
+def test_struct_layout_matches_header(tmp_path):
+    """The ctypes mirror of npl_linear_args / npl_rope_kv has the C layout."""
+    import shutil
+    import subprocess
+    from nanopointllm_b200 import _lib
+    cxx = shutil.which("g++") or shutil.which("gcc")
+    if cxx is None:
+        import pytest
+        pytest.skip("no host C compiler")
+    src = tmp_path / "layout.c"
+    src.write_text('#include <stdio.h>\n#include <stddef.h>\n#include "npl_w8a8.h"\n'
+                   'int main(void){printf("%zu %zu %zu %zu\\n", sizeof(npl_linear_args), sizeof(npl_rope_kv),'
+                   ' offsetof(npl_linear_args, rope), offsetof(npl_linear_args, absmax_out));return 0;}\n')
+    exe = tmp_path / "layout"
+    subprocess.run([cxx, "-x", "c", f"-I{REPO / 'include'}", str(src), "-o", str(exe)], check=True)
+    got = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split()
+    assert [int(v) for v in got] == [ctypes.sizeof(_lib.NplLinearArgs), ctypes.sizeof(_lib.NplRopeKV),
+                                     _lib.NplLinearArgs.rope.offset, _lib.NplLinearArgs.absmax_out.offset]
