@@ -117,9 +117,11 @@ __global__ void rope_store_kernel(const __half* __restrict__ qkv, int ld_qkv, in
 // partials into out[b, h]; with q_out given, the CTA that completes the last
 // head of b quantises the attention row of b per token (w8a8.py:106-115),
 // which is the input of the O projection.
+// 3 CTAs x ~69 KB per SM (64-token stages, 2-stage rings): measured the
+// fastest split on B200 (2 CTAs x 3 stages and 32-token stages were slower).
 constexpr int kAttnTok = 64;
 constexpr int kAttnStages = 2;
-constexpr int kAttnCtasPerSm = 3;  // 3 x ~66 KB of shared memory per SM
+constexpr int kAttnCtasPerSm = 3;
 constexpr int kAttnChunk = 256;
 constexpr int kAttnConsumers = 128;
 constexpr int kAttnThreads = 32 + kAttnConsumers;
