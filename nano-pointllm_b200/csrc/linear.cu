@@ -21,16 +21,23 @@
 //              [NT x 128 B] for int8 activations) per stage, 128-byte swizzle,
 //              a ring of 3-12 stages in shared memory
 //   warp 1     TMEM owner + MMA issuer (one thread): 4 MMAs of K = 32 per
-//              stage into a double-buffered int32 accumulator in TMEM
+//              stage into a ring of 2-4 int32 accumulators in TMEM
 //   warps 2-5  before the main loop: quantise fp16 activations (with RMSNorm)
 //              into per-unit token tiles in shared memory; then the epilogue:
 //              tcgen05.ld (TMEM lane = weight row, column = token), dequant
 //              ((acc * sa) * sw + bias) and the fused tail
 //
-// Work split ("stream-K"): the (tile, k-block) units of the whole problem are
-// divided evenly over the grid. A CTA that owns a whole tile runs its
-// epilogue from TMEM; partial tiles are reduced through int32 atomics in the
-// caller's workspace (exact and order-independent), and the CTA whose
+// Work split, decode tiles (NT <= 64): cluster split-K. Each tile's k-blocks
+// are shared by the S CTAs of one thread-block cluster (S <= 8, chosen per
+// shape); clusters take tiles round-robin. The non-leader CTAs add their
+// int32 partial tiles into the leader's shared memory with one bulk DSMEM
+// reduction each, so the cross-CTA reduction never leaves the GPC.
+//
+// Work split, prefill tiles (NT >= 128), and the fallback when the clusters
+// do not fit at once: stream-K. The (tile, k-block) units of the whole
+// problem are divided evenly over the grid. A CTA that owns a whole tile runs
+// its epilogue from TMEM; partial tiles are reduced through int32 atomics in
+// the caller's workspace (exact and order-independent), and the CTA whose
 // k-blocks complete the count runs the epilogue and clears the workspace.
 // Only a tile cut by a CTA boundary is partial, so the workspace holds
 // grid - 1 tile slots; a partial tile uses the slot of the first boundary
@@ -43,6 +50,8 @@
 
 #include <algorithm>
 #include <initializer_list>
+#include <mutex>
+#include <vector>
 
 #include "npl_common.cuh"
 
@@ -53,6 +62,7 @@ constexpr int kTileN = 128;   // weight rows per tile (MMA M)
 constexpr int kBlockK = 128;  // K bytes per stage (one 128-byte swizzle atom)
 constexpr int kThreads = 192;
 constexpr int kMaxStages = 12;
+constexpr int kMaxAccBufs = 4;
 constexpr int kCoresidentSmem = 110 * 1024;  // two CTAs per SM (programmatic dependent launch)
 constexpr int kMaxSmem = 226 * 1024;
 
@@ -88,9 +98,13 @@ struct LinearArgs {
   int n_tiles;
   int k_blocks;
   long long total_units;
+  int split;      // > 0: cluster split-K with `split` CTAs per cluster; 0: stream-K
+  int clusters;   // cluster split-K: number of clusters (tile stride)
+  int tiles;      // m_tiles * n_tiles
+  int red_bufs;   // cluster split-K: partial-tile buffers (1 or 2)
   int stages;
   int x_slots;
-  uint32_t off_a, off_b, off_x, off_f;
+  uint32_t off_a, off_b, off_x, off_f, off_r;
   int32_t* ws_acc;   // [grid - 1 slots][NT][128]
   int32_t* ws_cnt;   // [grid - 1 slots]
   int32_t* ws_xcnt;  // [1]: CTAs done reading x_absmax
@@ -102,18 +116,25 @@ struct LinearArgs {
 struct LinearCtl {
   uint64_t full[kMaxStages];
   uint64_t empty[kMaxStages];
-  uint64_t tfull[2];
-  uint64_t tempty[2];
+  uint64_t tfull[kMaxAccBufs];
+  uint64_t tempty[kMaxAccBufs];
   uint64_t teardown;
   uint64_t xready;
+  uint64_t rfull[2];  // cluster leader: contributors' partials of buffer b landed
+  uint64_t rfree[2];  // cluster contributor: leader consumed buffer b
   uint32_t tmem_base;
   int last_flag;
   __half xchg[8][kTileN];  // epilogue exchange between TMEM lanes
 };
 
+// TMEM accumulator ring depth: decode tiles keep 4 accumulators so that the
+// MMAs run up to 3 tiles ahead of an epilogue that waits for its cluster;
+// prefill tiles (NT >= 128) keep 2 (the 512 TMEM columns bound 2 x 256).
+__host__ __device__ constexpr int acc_bufs_for(int nt) { return nt <= 64 ? 4 : 2; }
+
 __host__ __device__ constexpr uint32_t tmem_cols_for(int nt) {
   uint32_t c = 32;
-  while (c < 2u * (uint32_t)nt) c <<= 1;
+  while (c < (uint32_t)(acc_bufs_for(nt) * nt)) c <<= 1;
   return c;
 }
 
@@ -129,16 +150,55 @@ __device__ __forceinline__ int atomic_add_acq_rel(int32_t* p, int v) {
   return old;
 }
 
-// Iterates the CTA's stream-K segments: (tile, kb0, kb1).
+// Rank of this CTA in its cluster and the k-block range [lo, hi) it owns in
+// every tile of the cluster split-K schedule (clusters are consecutive CTAs
+// along x).
+struct SplitRange {
+  int rank, lo, hi;
+  __device__ explicit SplitRange(const LinearArgs& p) {
+    const int s = max(p.split, 1);
+    rank = (int)(blockIdx.x % (unsigned)s);
+    lo = rank * p.k_blocks / s;
+    hi = (rank + 1) * p.k_blocks / s;
+  }
+};
+
+// Iterates the CTA's segments (tile, kb0, kb1).
+//   stream-K (split == 0): the CTA's contiguous share of the (tile, k-block)
+//     units, cut at tile boundaries;
+//   cluster split-K: tiles cluster, cluster + clusters, ... with the k-block
+//     range of the CTA's rank.
 struct SegmentIter {
   long long u, u1;
   int k_blocks;
-  __device__ SegmentIter(const LinearArgs& p) {
-    u = (long long)blockIdx.x * p.total_units / gridDim.x;
-    u1 = (long long)(blockIdx.x + 1) * p.total_units / gridDim.x;
+  int tile_next, tile_step, tiles, lo, hi;
+  bool split;
+  __device__ explicit SegmentIter(const LinearArgs& p) {
     k_blocks = p.k_blocks;
+    split = p.split > 0;
+    if (split) {
+      const SplitRange r(p);
+      tile_next = (int)(blockIdx.x / (unsigned)p.split);
+      tile_step = p.clusters;
+      tiles = p.tiles;
+      lo = r.lo;
+      hi = r.hi;
+      u = u1 = 0;
+    } else {
+      u = (long long)blockIdx.x * p.total_units / gridDim.x;
+      u1 = (long long)(blockIdx.x + 1) * p.total_units / gridDim.x;
+      tile_next = tile_step = tiles = lo = hi = 0;
+    }
   }
   __device__ bool next(int& tile, int& kb0, int& kb1) {
+    if (split) {
+      if (tile_next >= tiles) return false;
+      tile = tile_next;
+      tile_next += tile_step;
+      kb0 = lo;
+      kb1 = hi;
+      return true;
+    }
     if (u >= u1) return false;
     tile = (int)(u / k_blocks);
     kb0 = (int)(u % k_blocks);
@@ -148,10 +208,33 @@ struct SegmentIter {
   }
 };
 
-__device__ __forceinline__ float dequant(int32_t acc, float sa, float sw, const float* bias, int n) {
+// ((acc * sa) * sw) + bias_v, the bias added only when the layer has one.
+__device__ __forceinline__ float dequant(int32_t acc, float sa, float sw, const float* bias, float bias_v) {
   float v = __fmul_rn(__fmul_rn(__int2float_rn(acc), sa), sw);
-  if (bias) v = __fadd_rn(v, bias[n]);
+  if (bias) v = __fadd_rn(v, bias_v);
   return v;
+}
+
+// Per-row epilogue operands, loaded before the accumulator is ready: the
+// weight scale and bias of the row, and the residual of the first 8 tokens.
+struct EpiOperands {
+  float sw, bias;
+  __half res[8];
+};
+
+template <int NT>
+__device__ __forceinline__ void load_epi_operands(const LinearArgs& p, int m_tile, int n_tile, int row,
+                                                  EpiOperands& e) {
+  const int n = n_tile * kTileN + row;
+  e.sw = n < p.N ? p.sw[n] : 0.f;
+  e.bias = (p.bias && n < p.N) ? p.bias[n] : 0.f;
+  if (p.epilogue == NPL_EPI_RESIDUAL) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int m = m_tile * NT + j;
+      e.res[j] = (m < p.M && n < p.N) ? p.residual[(size_t)m * p.ld_res + n] : __float2half_rn(0.f);
+    }
+  }
 }
 
 // silu(g) rounded once to fp16, evaluated in fp64.
@@ -168,7 +251,8 @@ __device__ __forceinline__ void atomic_max_nonneg(int32_t* p, float v) {
 // `sa` holds the per-token activation scales indexed by token.
 template <int NT>
 __device__ __forceinline__ void epilogue_chunk(const LinearArgs& p, LinearCtl& c, const float* sa, int m_tile,
-                                               int n_tile, int row, int c0, const int32_t (&acc)[8]) {
+                                               int n_tile, int row, int c0, const int32_t (&acc)[8],
+                                               const EpiOperands& e) {
   const int n = n_tile * kTileN + row;
   const int m_base = m_tile * NT + c0;
   const int lane = threadIdx.x & 31;
@@ -179,12 +263,12 @@ __device__ __forceinline__ void epilogue_chunk(const LinearArgs& p, LinearCtl& c
   }
   if (p.epilogue == NPL_EPI_SILU_MUL) {
     // rows 0-63 gate, 64-127 up of output columns n_tile*64 + (row % 64)
-    const float sw = p.sw[n];
+    const float sw = e.sw;
     if (row >= 64) {
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const int m = min(m_base + j, p.M - 1);
-        c.xchg[j][row - 64] = __float2half_rn(dequant(acc[j], sa[m], sw, p.bias, n));
+        c.xchg[j][row - 64] = __float2half_rn(dequant(acc[j], sa[m], sw, p.bias, e.bias));
       }
     }
     epi_bar();
@@ -196,7 +280,7 @@ __device__ __forceinline__ void epilogue_chunk(const LinearArgs& p, LinearCtl& c
         const int m = m_base + j;
         float h = 0.f;
         if (m < p.M) {
-          const float g = __half2float(__float2half_rn(dequant(acc[j], sa[m], sw, p.bias, n)));
+          const float g = __half2float(__float2half_rn(dequant(acc[j], sa[m], sw, p.bias, e.bias)));
           const float u = __half2float(c.xchg[j][row]);
           const __half hh = __float2half_rn(__fmul_rn(silu_h(g), u));
           out[(size_t)m * p.ld_out + col] = hh;
@@ -214,11 +298,11 @@ __device__ __forceinline__ void epilogue_chunk(const LinearArgs& p, LinearCtl& c
   if (p.epilogue == NPL_EPI_ROPE_KV) {
     // every tile lies in one of q | k | v (head blocks are multiples of 128)
     const int D = p.head_dim, half_d = D / 2;
-    const float sw = p.sw[n];
+    const float sw = e.sw;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const int m = min(m_base + j, p.M - 1);
-      c.xchg[j][row] = __float2half_rn(dequant(acc[j], sa[m], sw, p.bias, n));
+      c.xchg[j][row] = __float2half_rn(dequant(acc[j], sa[m], sw, p.bias, e.bias));
     }
     epi_bar();
     const int q_cols = p.heads * D, k_cols = p.kv_heads * D;
@@ -253,15 +337,15 @@ __device__ __forceinline__ void epilogue_chunk(const LinearArgs& p, LinearCtl& c
     return;
   }
   if (n >= p.N) return;
-  const float sw = p.sw[n];
+  const float sw = e.sw;
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
     const int m = m_base + j;
     if (m >= p.M) break;
-    const float v = dequant(acc[j], sa[m], sw, p.bias, n);
+    const float v = dequant(acc[j], sa[m], sw, p.bias, e.bias);
     if (p.epilogue == NPL_EPI_RESIDUAL) {
       const float o = __half2float(__float2half_rn(v));
-      const float r = __half2float(p.residual[(size_t)m * p.ld_res + n]);
+      const float r = __half2float(c0 == 0 ? e.res[j] : p.residual[(size_t)m * p.ld_res + n]);
       static_cast<__half*>(p.out)[(size_t)m * p.ld_out + n] = __float2half_rn(__fadd_rn(o, r));
     } else if (p.out_dtype == NPL_F32) {
       static_cast<float*>(p.out)[(size_t)m * p.ld_out + n] = v;
@@ -384,9 +468,20 @@ __device__ void produce_activations(const LinearArgs& p, int8_t* xslot, float* s
     for (int m = ct; m < p.M; m += 128) s_scale[m] = scale_from_absmax(__int_as_float(p.x_absmax[m]));
     epi_bar();
   }
-  const long long u_begin = (long long)blockIdx.x * p.total_units / gridDim.x;
-  const long long u_end = (long long)(blockIdx.x + 1) * p.total_units / gridDim.x;
-  const int total = (int)(u_end - u_begin) * NT * 8;
+  // Token tile slots: stream-K keeps one per unit of the CTA (slot u holds
+  // k-block (u_begin + u) % k_blocks); cluster split-K one per k-block of the
+  // CTA's range, shared by all its tiles (there is one token tile row).
+  long long u_begin;
+  int n_slots;
+  if (p.split > 0) {
+    const SplitRange r(p);
+    u_begin = r.lo;
+    n_slots = r.hi - r.lo;
+  } else {
+    u_begin = (long long)blockIdx.x * p.total_units / gridDim.x;
+    n_slots = (int)((long long)(blockIdx.x + 1) * p.total_units / gridDim.x - u_begin);
+  }
+  const int total = n_slots * NT * 8;
   const bool norm = p.x_mode == NPL_X_F16_RMSNORM;
   constexpr int kBatch = 4;
   for (int base_item = ct; base_item < total; base_item += 128 * kBatch) {
@@ -438,7 +533,9 @@ __device__ void produce_activations(const LinearArgs& p, int8_t* xslot, float* s
   fence_proxy_async_smem();  // the tensor cores read these tiles through the async proxy
 }
 
-template <int NT>
+// kXF16: the fp16-activation modes (their prologue costs registers, so the
+// int8-activation kernel is compiled without it).
+template <int NT, bool kXF16>
 __global__ void __launch_bounds__(kThreads, 1)
     w8a8_linear_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                        const LinearArgs p) {
@@ -452,8 +549,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   float* s_scale = reinterpret_cast<float*>(base + p.off_f);
   float* s_inv = s_scale + NT;
   constexpr uint32_t kTmemCols = tmem_cols_for(NT);
+  constexpr int kAccBufs = acc_bufs_for(NT);
   constexpr uint32_t kIdesc = idesc_i8(kTileN, NT);
-  const bool x_int8 = p.x_mode == NPL_X_INT8;
+  constexpr bool x_int8 = !kXF16;
   const uint32_t stage_bytes = kTileN * kBlockK + (x_int8 ? NT * kBlockK : 0);
   const int stages = p.stages;
 
@@ -467,13 +565,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&c.full[i], 1);
       mbar_init(&c.empty[i], 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kAccBufs; ++i) {
       mbar_init(&c.tfull[i], 1);
       mbar_init(&c.tempty[i], 4);
     }
     mbar_init(&c.teardown, 1);
     mbar_init(&c.xready, 128);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&c.rfull[i], 1);
+      mbar_init(&c.rfree[i], 1);
+    }
     fence_mbar_init();
+  }
+  const bool clustered = p.split > 1;
+  int32_t* red = reinterpret_cast<int32_t*>(base + p.off_r);
+  if (clustered) {
+    // the leader's partial-tile buffers start at zero: contributors add into
+    // them through the async proxy
+    for (int i = threadIdx.x; i < p.red_bufs * NT * kTileN; i += kThreads) red[i] = 0;
+    fence_proxy_async_smem();
   }
   if (warp == 1) {
     tmem_alloc(&c.tmem_base, kTmemCols);
@@ -483,6 +593,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = c.tmem_base;
+  // Barriers and buffers of every CTA of the cluster are initialised before
+  // any CTA reaches into another (each role waits where it first needs it).
+  if (clustered) {
+    cluster_arrive_release();
+    if (threadIdx.x != 0) cluster_wait_acquire();  // thread 0 (TMA) waits after its first weight loads
+  }
   pdl_trigger();  // the next kernel may start launching its CTAs
 
   if (warp == 0) {
@@ -492,7 +608,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t pol_x = policy_evict_last();
       // Weights do not depend on earlier kernels: the weight tiles of the
       // first ring stages are requested before waiting for the previous
-      // kernel; the token tiles (its output) only after.
+      // kernel; the token tiles (its output) only after. (Prefetching further
+      // weight tiles into L2 here was measured slower on B200: the requests
+      // delay the previous kernel's completion and this kernel's token loads.)
       int pre = 0;
       {
         SegmentIter it(p);
@@ -507,6 +625,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       uint32_t outstanding = (1u << pre) - 1;  // stages holding a load (pre <= 12)
+      if (clustered) cluster_wait_acquire();
       pdl_wait();
       SegmentIter it(p);
       int tile, kb0, kb1, stage = 0, unit = 0;
@@ -550,8 +669,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       int tile, kb0, kb1, stage = 0, seg = 0, unit = 0;
       uint32_t phase = 0;
       while (ok && it.next(tile, kb0, kb1)) {
-        const int buf = seg & 1;
-        const uint32_t tphase = (seg >> 1) & 1;
+        const int buf = seg % kAccBufs;
+        const uint32_t tphase = (seg / kAccBufs) & 1;
         if (!mbar_wait(&c.tempty[buf], tphase ^ 1, p.status, NPL_DEV_TIMEOUT_MMA)) break;
         tc_fence_after();
         const uint32_t d = tmem_base + (uint32_t)(buf * NT);
@@ -562,8 +681,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tc_fence_after();
           const uint32_t a0 = smem_u32(ring_a + (size_t)stage * kTileN * kBlockK);
+          const int xs = p.split > 0 ? kb - kb0 : unit;  // token tile slot (see produce_activations)
           const uint32_t b0 = x_int8 ? smem_u32(ring_b + (size_t)stage * NT * kBlockK)
-                                     : smem_u32(xslot + (size_t)unit * NT * kBlockK);
+                                     : smem_u32(xslot + (size_t)xs * NT * kBlockK);
 #pragma unroll
           for (int kk = 0; kk < kBlockK / 32; ++kk) {
             mma_i8(d, sdesc_k_sw128(a0 + kk * 32), sdesc_k_sw128(b0 + kk * 32), kIdesc,
@@ -589,7 +709,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row = quarter * 32 + lane;
     const int ct = threadIdx.x - 64;
     pdl_wait();
-    if (!x_int8) {
+    if constexpr (kXF16) {
       produce_activations<NT>(p, xslot, s_scale, s_inv, reinterpret_cast<double*>(s_inv + NT), ct);
       mbar_arrive(&c.xready);
       if (p.x_mode == NPL_X_F16_ABSMAX) {
@@ -602,16 +722,86 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-    const float* sa = x_int8 ? p.sa : s_scale;
+    // per-token activation scales from shared memory when there is one token
+    // tile (decode); int8 activations bring theirs from global memory
+    const float* sa = s_scale;
+    if (x_int8) {
+      if (p.M <= NT) {
+        for (int m = ct; m < p.M; m += 128) s_scale[m] = p.sa[m];
+        epi_bar();
+      } else {
+        sa = p.sa;
+      }
+    }
+    // Cluster split-K: rank 0 leads every tile of the cluster. The other
+    // ranks add their partial accumulator, straight from registers, into the
+    // leader's buffer in its shared memory (red.async, counted in bytes on the
+    // leader's rfull barrier); the leader adds its own TMEM accumulator,
+    // clears the buffer and runs the epilogue. Buffer rb is handed back to the
+    // contributors (rfree) once cleared, when a later tile of the cluster
+    // needs it.
+    const SplitRange sr(p);
+    const bool leader = sr.rank == 0;
+    const uint32_t red_bytes = (uint32_t)(NT * kTileN * sizeof(int32_t));
+    const int cluster_tiles =
+        clustered ? (p.tiles - (int)(blockIdx.x / (unsigned)p.split) + p.clusters - 1) / p.clusters : 0;
     SegmentIter it(p);
     int tile, kb0, kb1, seg = 0;
     while (it.next(tile, kb0, kb1)) {
-      const int buf = seg & 1;
-      const uint32_t tphase = (seg >> 1) & 1;
+      const int buf = seg % kAccBufs;
+      const uint32_t tphase = (seg / kAccBufs) & 1;
       const int m_tile = tile / p.n_tiles, n_tile = tile % p.n_tiles;
+      const bool contributor = clustered && !leader;
+      EpiOperands eo;
+      if (!contributor) load_epi_operands<NT>(p, m_tile, n_tile, row, eo);
       if (!mbar_wait(&c.tfull[buf], tphase, p.status, NPL_DEV_TIMEOUT_EPILOGUE)) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(buf * NT);
+      if (clustered) {
+        const int rb = seg % p.red_bufs, use = seg / p.red_bufs;
+        int32_t* rbuf = red + (size_t)rb * NT * kTileN;  // [NT][128]: column = token, row = weight row
+        if (leader) {
+          if (ct == 0) mbar_arrive_expect_tx(&c.rfull[rb], (uint32_t)(p.split - 1) * red_bytes);
+          mbar_wait_cluster(&c.rfull[rb], use & 1, p.status, NPL_DEV_TIMEOUT_EPILOGUE);
+          for (int c0 = 0; c0 < NT; c0 += 8) {
+            int32_t acc[8];
+            tmem_ld_x8(taddr + c0, acc);
+            tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              int32_t* cell = rbuf + (c0 + j) * kTileN + row;
+              acc[j] += *cell;  // int32 sums are exact in any order
+              *cell = 0;
+            }
+            epilogue_chunk<NT>(p, c, sa, m_tile, n_tile, row, c0, acc, eo);
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&c.tempty[buf]);
+          if (seg + p.red_bufs < cluster_tiles) {
+            fence_proxy_async_smem();  // the cleared cells, before the contributors' next adds
+            epi_bar();
+            if (ct > 0 && ct < p.split) mbar_arrive_remote(cluster_map(&c.rfree[rb], (uint32_t)ct));
+          }
+        } else {
+          if (seg >= p.red_bufs) mbar_wait_cluster(&c.rfree[rb], (use - 1) & 1, p.status, NPL_DEV_TIMEOUT_EPILOGUE);
+          const uint32_t dst = cluster_map(rbuf + row, 0);
+          const uint32_t bar = cluster_map(&c.rfull[rb], 0);
+          for (int c0 = 0; c0 < NT; c0 += 8) {
+            int32_t acc[8];
+            tmem_ld_x8(taddr + c0, acc);
+            tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              red_add_s32_cluster(dst + (uint32_t)((c0 + j) * kTileN * sizeof(int32_t)), acc[j], bar);
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&c.tempty[buf]);
+        }
+        ++seg;
+        continue;
+      }
       const bool whole = (kb0 == 0 && kb1 == p.k_blocks);
       // slot = (first CTA boundary strictly inside the tile) - 1
       const long long first_unit = (long long)tile * p.k_blocks;
@@ -622,7 +812,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           int32_t acc[8];
           tmem_ld_x8(taddr + c0, acc);
           tmem_wait_ld();
-          epilogue_chunk<NT>(p, c, sa, m_tile, n_tile, row, c0, acc);
+          epilogue_chunk<NT>(p, c, sa, m_tile, n_tile, row, c0, acc, eo);
         }
       } else {
         for (int c0 = 0; c0 < NT; c0 += 8) {
@@ -651,7 +841,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               acc[j] = __ldcg(cell);
               __stcg(cell, 0);
             }
-            epilogue_chunk<NT>(p, c, sa, m_tile, n_tile, row, c0, acc);
+            epilogue_chunk<NT>(p, c, sa, m_tile, n_tile, row, c0, acc, eo);
           }
           if (ct == 0) p.ws_cnt[slot] = 0;
         }
@@ -667,6 +857,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
   }
+  // No CTA of a cluster waits for the others at exit: the leader's buffers
+  // and barriers are last written by the adds its final rfull wait counted,
+  // and a contributor's barriers are only signalled while it waits on them.
 }
 
 // ------------------------------------------------------------------ host
@@ -726,32 +919,136 @@ size_t ws_bytes(int M) {
 
 constexpr uint32_t align1k(size_t x) { return (uint32_t)((x + 1023) & ~size_t(1023)); }
 
+// Clusters of `split` CTAs of `kern` with `smem` bytes that fit on the
+// device at once (cached per device, kernel, shared memory and size).
+int max_active_clusters(const void* kern, int smem, int split) {
+  struct Entry {
+    int dev;
+    const void* kern;
+    int smem, split, n;
+  };
+  static std::mutex mu;
+  static std::vector<Entry> cache;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  std::lock_guard<std::mutex> lock(mu);
+  for (const Entry& e : cache)
+    if (e.dev == dev && e.kern == kern && e.smem == smem && e.split == split) return e.n;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)split);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = (size_t)smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)split;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+    (void)cudaGetLastError();
+    n = 0;
+  }
+  cache.push_back({dev, kern, smem, split, n});
+  return n;
+}
+
+// Shared memory that leaves room for one CTA per SM only: the cluster
+// capacity at this size is the number of clusters that fit with every CTA on
+// an SM of its own. (GPCs differ in size, so on B200 clusters of 3 or 4 fit
+// on fewer than all 148 SMs: placing more doubles CTAs up on some SMs.)
+constexpr int kOnePerSmSmem = 120 * 1024;
+
+struct Schedule {
+  int split;     // 0: stream-K; >= 1: CTAs per tile (cluster size)
+  int clusters;  // cluster split-K: clusters in the grid
+};
+
+// Decode tiles: cluster split-K with S CTAs per tile (S <= 8) and C clusters
+// (C <= the clusters that fit one CTA per SM), or stream-K over all SMs,
+// whichever has the least per-CTA work in (tile, k-block) units. Stream-K's
+// global partial-tile reduction costs about 3 units more than the DSMEM one
+// (measured on B200: ~1 us against 0.35 us per 16 KB weight unit).
+constexpr int kStreamKFixupUnits = 3;
+
+Schedule pick_schedule(const void* kern, int tiles, int k_blocks, long long units, int grid_max) {
+  Schedule best{0, 0};
+  long long best_cost = (units + grid_max - 1) / grid_max + kStreamKFixupUnits;
+  for (int s = 1; s <= 8 && s <= k_blocks; ++s) {
+    const int cap = s == 1 ? grid_max : max_active_clusters(kern, kOnePerSmSmem, s);
+    const int c = std::min(tiles, std::min(cap, grid_max / s));
+    if (c < 1) continue;
+    const long long cost = (long long)((tiles + c - 1) / c) * ((k_blocks + s - 1) / s);
+    if (cost < best_cost) {
+      best_cost = cost;
+      best = {s, c};
+    }
+  }
+  return best;
+}
+
+// Shared-memory layout for the schedule in `p` (split, x_slots); returns the
+// dynamic shared memory size, or 0 when the stage ring does not fit.
 template <int NT>
-int launch_linear(const CUtensorMap& tw, const CUtensorMap& tx, LinearArgs& p, int grid, cudaStream_t st) {
-  auto kern = w8a8_linear_kernel<NT>;
+int layout_linear(LinearArgs& p) {
   const bool x_int8 = p.x_mode == NPL_X_INT8;
   const size_t stage_bytes = (size_t)kTileN * kBlockK + (x_int8 ? (size_t)NT * kBlockK : 0);
   const size_t xslots = x_int8 ? 0 : (size_t)p.x_slots * NT * kBlockK;
+  const size_t reds = (size_t)p.red_bufs * NT * kTileN * sizeof(int32_t);
+  const size_t tail = 2 * NT * sizeof(float) + 8 * sizeof(double);
   p.off_a = align1k(sizeof(LinearCtl));
   // Decode tiles (NT <= 64) keep the CTA near 110 KB when they can, so that
   // the next kernel's CTA fits beside it on an SM and starts its weight loads
   // while this one finishes; prefill tiles take the whole shared memory.
-  const size_t fixed = p.off_a + xslots + 2 * NT * sizeof(float) + 8 * sizeof(double) + 1024 + 1024;
+  const size_t fixed = p.off_a + xslots + reds + tail + 1024 + 1024;
   int stages = 0;
   if (NT <= 64 && fixed + 3 * stage_bytes <= (size_t)kCoresidentSmem)
     stages = (int)std::min<size_t>(6, (kCoresidentSmem - fixed) / stage_bytes);
   else if (fixed + 2 * stage_bytes <= (size_t)kMaxSmem)
     stages = (int)std::min<size_t>(kMaxStages, (kMaxSmem - fixed) / stage_bytes);
-  if (stages < 2)
-    return fail(NPL_ERR_UNSUPPORTED, "npl_w8a8_linear: %d fp16 token tiles do not fit in shared memory", p.x_slots);
+  if (stages < 2) return 0;
   p.stages = stages;
   p.off_b = p.off_a + (uint32_t)(stages * kTileN * kBlockK);
   p.off_x = p.off_b + (uint32_t)(x_int8 ? stages * NT * kBlockK : 0);
-  p.off_f = p.off_x + (uint32_t)xslots;
-  const int smem = (int)(p.off_f + 2 * NT * sizeof(float) + 8 * sizeof(double) + 1024);
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+  p.off_r = p.off_x + (uint32_t)xslots;  // 1 KB aligned: stage and slot sizes are multiples of 1 KB
+  p.off_f = p.off_r + (uint32_t)reds;
+  return (int)(p.off_f + tail + 1024);
+}
+
+template <int NT>
+int launch_linear(const CUtensorMap& tw, const CUtensorMap& tx, LinearArgs& p, cudaStream_t st) {
+  const bool x_int8 = p.x_mode == NPL_X_INT8;
+  auto kern = x_int8 ? w8a8_linear_kernel<NT, false> : w8a8_linear_kernel<NT, true>;
+  const int grid_max = max_grid();
+  const void* kfn = reinterpret_cast<const void*>(kern);
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem) != cudaSuccess)
     return launch_status("npl_w8a8_linear: smem attribute");
-  return launch_pdl("npl_w8a8_linear", kern, dim3((unsigned)grid), dim3(kThreads), (size_t)smem, st, tw, tx, p);
+  int smem = 0, grid = 0;
+  if (NT <= 64) {
+    const Schedule s = pick_schedule(kfn, p.tiles, p.k_blocks, p.total_units, grid_max);
+    if (s.split > 0) {
+      p.split = s.split;
+      p.clusters = s.clusters;
+      p.red_bufs = s.split > 1 ? (NT <= 16 ? 2 : 1) : 0;
+      p.x_slots = (p.k_blocks + s.split - 1) / s.split;
+      smem = layout_linear<NT>(p);
+      // the schedule has no second wave: all clusters must be resident at once
+      if (smem && p.split > 1 && max_active_clusters(kfn, smem, p.split) < p.clusters) smem = 0;
+      grid = p.clusters * p.split;
+    }
+  }
+  if (!smem) {  // stream-K
+    p.split = p.clusters = p.red_bufs = 0;
+    grid = (int)std::min<long long>(grid_max, p.total_units);
+    p.x_slots = (int)((p.total_units + grid - 1) / grid);
+    smem = layout_linear<NT>(p);
+    if (!smem)
+      return fail(NPL_ERR_UNSUPPORTED, "npl_w8a8_linear: %d fp16 token tiles do not fit in shared memory",
+                  p.x_slots);
+  }
+  return launch_pdl_cluster("npl_w8a8_linear", kern, dim3((unsigned)grid), dim3(kThreads), (size_t)smem, st,
+                            (unsigned)std::max(p.split, 1), tw, tx, p);
 }
 
 struct LinearCall {
@@ -874,9 +1171,8 @@ int run_linear(const LinearCall& a, void* workspace, size_t workspace_bytes, voi
   p.k_blocks = (K + kBlockK - 1) / kBlockK;
   const int m_tiles = (M + nt - 1) / nt;
   p.total_units = (long long)p.n_tiles * m_tiles * p.k_blocks;
+  p.tiles = p.n_tiles * m_tiles;
   p.status = device_status_ptr();
-  const int grid = (int)std::min<long long>(max_grid(), p.total_units);
-  p.x_slots = (int)((p.total_units + grid - 1) / grid);
 
   CUtensorMap tw, tx;
   if (int rc = make_map(&tw, a.qw, N, K, a.ldw, kTileN)) return rc;
@@ -887,12 +1183,12 @@ int run_linear(const LinearCall& a, void* workspace, size_t workspace_bytes, voi
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   switch (nt) {
-    case 8: return launch_linear<8>(tw, tx, p, grid, st);
-    case 16: return launch_linear<16>(tw, tx, p, grid, st);
-    case 32: return launch_linear<32>(tw, tx, p, grid, st);
-    case 64: return launch_linear<64>(tw, tx, p, grid, st);
-    case 128: return launch_linear<128>(tw, tx, p, grid, st);
-    default: return launch_linear<256>(tw, tx, p, grid, st);
+    case 8: return launch_linear<8>(tw, tx, p, st);
+    case 16: return launch_linear<16>(tw, tx, p, st);
+    case 32: return launch_linear<32>(tw, tx, p, st);
+    case 64: return launch_linear<64>(tw, tx, p, st);
+    case 128: return launch_linear<128>(tw, tx, p, st);
+    default: return launch_linear<256>(tw, tx, p, st);
   }
 }
 

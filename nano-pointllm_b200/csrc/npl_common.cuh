@@ -34,25 +34,40 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 // before touching any global memory the previous kernels read or write
 // (constant weights excepted), and calls pdl_trigger() to let the next kernel
 // start early in turn.
+// `cluster_x` > 1 launches thread-block clusters of that many consecutive
+// CTAs along x (grid.x must be a multiple of it).
 template <typename... KArgs, typename... Args>
-int launch_pdl(const char* what, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
-               Args&&... args) {
+int launch_pdl_cluster(const char* what, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t st, unsigned cluster_x, Args&&... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  if (cluster_x > 1) {
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = cluster_x;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.numAttrs = 2;
+  }
   const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
   if (e != cudaSuccess) {
     (void)cudaGetLastError();
     return fail(NPL_ERR_LAUNCH, "%s: %s", what, cudaGetErrorString(e));
   }
   return NPL_OK;
+}
+
+template <typename... KArgs, typename... Args>
+int launch_pdl(const char* what, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+               Args&&... args) {
+  return launch_pdl_cluster(what, kernel, grid, block, smem, st, 1u, static_cast<Args&&>(args)...);
 }
 
 // ------------------------------------------------------------- device side
@@ -177,6 +192,65 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
       return false;
     }
   }
+}
+
+// ------------------------------------------------- thread-block clusters
+// Address of the same shared-memory location in CTA `rank` of the cluster
+// (a shared::cluster address).
+__device__ __forceinline__ uint32_t cluster_map(const void* local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(local)), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ void cluster_arrive_release() {
+  asm volatile("barrier.cluster.arrive.release;" ::: "memory");
+}
+
+__device__ __forceinline__ void cluster_wait_acquire() { asm volatile("barrier.cluster.wait.acquire;" ::: "memory"); }
+
+// One arrival on an mbarrier of another CTA of the cluster, ordered after this
+// thread's earlier writes at cluster scope.
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// mbar_wait for phases completed by other CTAs of the cluster (acquire at
+// cluster scope); bounded the same way.
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, int* status, int code) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    for (int i = 0; i < 64; ++i)
+      if (mbar_try_wait_cluster(bar, parity)) return true;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      if (status) atomicExch(status, code);
+      return false;
+    }
+  }
+}
+
+// s32 add of a register into another CTA's shared memory (DSMEM); completion
+// (4 bytes) is counted on the destination CTA's mbarrier. The source is a
+// register, so the issuing CTA may exit while the add is in flight.
+__device__ __forceinline__ void red_add_s32_cluster(uint32_t dst_cluster, int32_t v, uint32_t bar_cluster) {
+  asm volatile(
+      "red.async.relaxed.cluster.shared::cluster.mbarrier::complete_tx::bytes.add.s32 [%0], %1, [%2];" ::"r"(
+          dst_cluster),
+      "r"(v), "r"(bar_cluster)
+      : "memory");
 }
 
 // 2-D tiled TMA load into shared memory, completion counted on `bar`.
