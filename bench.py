@@ -166,7 +166,7 @@ def linear_bytes(m: int, n: int, k: int, out_cols: int, residual: bool, fp16_x: 
     return n * k + 4 * n + x + 2 * m * out_cols + (2 * m * out_cols if residual else 0)
 
 
-def op_bytes(shape, name: str, ctx_len: int) -> int:
+def op_bytes(shape, name: str, ctx_len: int, fused_mlp: bool = True) -> int:
     m, h, i_, v = BATCH, shape.hidden, shape.intermediate, shape.vocab
     qkv_n = (shape.heads + 2 * shape.kv_heads) * shape.head_dim
     if name == "linear.qkv":  # q out, k/v written to the cache (+ positions, slots, cos/sin rows)
@@ -175,8 +175,8 @@ def op_bytes(shape, name: str, ctx_len: int) -> int:
         return linear_bytes(m, h, shape.heads * shape.head_dim, h, True, False)
     if name == "linear.gate_up":
         return linear_bytes(m, 2 * i_, h, i_, False, False)
-    if name == "linear.down":
-        return linear_bytes(m, h, i_, h, True, False)
+    if name == "linear.down":  # fused: fp16 input rows, quantised in the kernel
+        return linear_bytes(m, h, i_, h, True, fused_mlp)
     if name == "linear.lm_head":
         return linear_bytes(m, v, h, v, False, False)
     if name == "attention":
@@ -313,12 +313,13 @@ def run_ours(args, torch, dist, rank: int, world: int, device) -> dict | None:
     peak, peak_kind = _peaks()
     lin_names = [n for n in per_op if n.startswith("linear.")]
     lin_ms = sum(sum(per_op[n]) for n in lin_names)
-    lin_bytes = sum(op_bytes(shape, n, ctx_mid) * len(per_op[n]) for n in lin_names)
+    fused = run.fuse_mlp_quant
+    lin_bytes = sum(op_bytes(shape, n, ctx_mid, fused) * len(per_op[n]) for n in lin_names)
     lin_launches = sum(len(per_op[n]) for n in lin_names)
     achieved = lin_bytes / (lin_ms * 1e-3) / 1e9
     kernels = {}
     for name, times in per_op.items():
-        b = op_bytes(shape, name, ctx_mid)
+        b = op_bytes(shape, name, ctx_mid, fused)
         avg = sum(times) / len(times)
         kernels[name] = {"launches_per_step": len(times) // n_eager, "avg_us": round(avg * 1e3, 2),
                          "share": None}
@@ -329,7 +330,7 @@ def run_ours(args, torch, dist, rank: int, world: int, device) -> dict | None:
     for name, times in per_op.items():
         kernels[name]["share"] = round(sum(times) / tot, 4)
 
-    launches_per_step = shape.layers * 9 + 2
+    launches_per_step = sum(len(t) for t in per_op.values()) // n_eager  # every op is one library kernel
     tokens = BATCH * world * args.steps
     value = tokens / (dev_ms * 1e-3)
     line = {

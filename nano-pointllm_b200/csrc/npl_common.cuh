@@ -74,6 +74,17 @@ int launch_pdl(const char* what, void (*kernel)(KArgs...), dim3 grid, dim3 block
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
+// The linear kernels read their weights before pdl_wait(): weights must not
+// be written by a kernel that may still be running. npl_quant_rows, which
+// quantises weights, therefore lets the next kernel launch only after its own
+// writes are visible: every thread of the CTA calls this after its last
+// global write (no thread may have exited early unless the whole CTA did).
+__device__ __forceinline__ void pdl_trigger_after_writes() {
+  __threadfence();
+  __syncthreads();
+  pdl_trigger();
+}
+
 // Error word shared by all kernels of the library on this device. A kernel
 // that gives up a bounded wait stores its NPL_DEV_* code here; the host reads
 // it with npl_device_status().

@@ -65,7 +65,6 @@ __global__ void __launch_bounds__(kQuantThreads) quant_rows_kernel(const T* __re
   __shared__ float red[32];
   constexpr int V = Vec<T>::N;
   pdl_wait();
-  pdl_trigger();
   const T* row = x + (size_t)blockIdx.x * ldx;
   float amax = 0.f;
   for (int c = threadIdx.x * V; c < cols; c += kQuantThreads * V) {
@@ -86,6 +85,7 @@ __global__ void __launch_bounds__(kQuantThreads) quant_rows_kernel(const T* __re
     for (int i = 0; i < V; ++i) qi[i] = quantize_one(v[i], s);
     store_q<V>(qrow + c, qi);
   }
+  pdl_trigger_after_writes();  // the rows may be weights, read by the next linear before its pdl_wait
 }
 
 // RMSNorm of one fp16 row (optionally x + residual) + per-token quantisation.

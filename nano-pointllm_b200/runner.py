@@ -121,9 +121,17 @@ class W8A8LlamaRunner:
     """
 
     def __init__(self, shape: LlamaShape, state_dict: dict[str, torch.Tensor], *, device: torch.device,
-                 kv_pool: torch.Tensor | None = None, num_blocks: int = 0, block_size: int = 256):
+                 kv_pool: torch.Tensor | None = None, num_blocks: int = 0, block_size: int = 256,
+                 fuse_mlp_quant: bool = False):
         self.shape = shape
         self.device = torch.device(device)
+        # fuse_mlp_quant, decode batches (<= 64 tokens): the gate/up epilogue
+        # also records each token's absmax of SiLU(gate)*up, and down quantises
+        # its fp16 input itself, so no separate quantisation kernel runs between
+        # them. Off by default: on B200 the in-kernel quantisation lengthens
+        # down's critical path by more than the separate kernel costs.
+        self.fuse_mlp_quant = fuse_mlp_quant
+        self._act_absmax = torch.zeros(64, dtype=torch.int32, device=self.device)
         if kv_pool is None:
             kv_pool = torch.zeros(2, shape.layers, num_blocks, block_size, shape.kv_heads, shape.head_dim,
                                   dtype=torch.float16, device=self.device)
@@ -228,6 +236,13 @@ class W8A8LlamaRunner:
         h2 = op("linear.o", W.linear_q, aq, asc, layer.o.qweight, layer.o.wscale,
                 epilogue=L.EPI_RESIDUAL, residual=h)
         xq, xs, _ = op("rmsnorm_quant", rmsnorm_quant, h2, layer.post_norm, s.eps)
+        m = h2.shape[0]
+        if self.fuse_mlp_quant and m <= self._act_absmax.numel():
+            # the absmax buffer is zero on entry and zeroed again by down
+            act = op("linear.gate_up", W.linear_ex, layer.gate_up.qweight, layer.gate_up.wscale, x_mode=L.X_INT8,
+                     m=m, qa=xq, sa=xs, epilogue=L.EPI_SILU_MUL, absmax_out=self._act_absmax)
+            return op("linear.down", W.linear_ex, layer.down.qweight, layer.down.wscale, x_mode=L.X_F16_ABSMAX,
+                      m=m, x_f16=act, x_absmax=self._act_absmax, epilogue=L.EPI_RESIDUAL, residual=h2)
         act = op("linear.gate_up", W.linear_q, xq, xs, layer.gate_up.qweight, layer.gate_up.wscale,
                  epilogue=L.EPI_SILU_MUL)
         aq, asc = op("quant", W.dynamic_per_token_quant, act)
