@@ -103,26 +103,32 @@ __global__ void rope_store_kernel(const __half* __restrict__ qkv, int ld_qkv, in
 }
 
 // ------------------------------------------------- paged decode attention
-// Persistent kernel, at most one CTA per SM, 160 threads:
-//   warp 0     producer: takes work items from a global counter, looks up the
-//              block table and streams the item's K and V through a ring of
+// Persistent kernel, 3 CTAs per SM, 160 threads:
+//   warp 0     producer: takes work items (the CTA's first item is blockIdx.x,
+//              later ones come from a global counter), looks up the block
+//              table and streams the item's K and V through a ring of
 //              64-token stages with TMA (3-D tensor maps over the cache viewed
 //              as [tokens][Hkv][D]; one box = min(64, block_size) tokens of
 //              one head)
 //   warps 1-4  consumers: D/8 lanes per token, 128/(D/8) token streams, each
 //              with its own online-softmax state over the item's tokens
-// A work item is (256-token chunk of the context, sequence b, head h). At the
-// end of an item the streams are merged into a partial (max, sum, acc[D]) in
-// the workspace; the CTA that completes the last chunk of (b, h) merges the
-// partials into out[b, h]; with q_out given, the CTA that completes the last
-// head of b quantises the attention row of b per token (w8a8.py:106-115),
-// which is the input of the O projection.
+// A work item is (chunk of the context, sequence b, head h); items are
+// numbered chunk-major, so at any time the CTAs read the same token rows of
+// many heads (adjacent 256-byte pieces of each 8 KB cache row), which keeps
+// the DRAM accesses local. At the end of an item the streams are merged into
+// a partial (max, sum, acc[D]); chunks before the last one of (b, h) publish
+// theirs behind a per-chunk flag that carries the launch epoch (the flags are
+// never reset), and the item of the last chunk merges them into out[b, h].
+// With q_out given, the CTA that completes the last head of b quantises the
+// attention row of b per token (w8a8.py:106-115), which is the input of the O
+// projection.
 // 3 CTAs x ~69 KB per SM (64-token stages, 2-stage rings): measured the
 // fastest split on B200 (2 CTAs x 3 stages and 32-token stages were slower).
 constexpr int kAttnTok = 64;
 constexpr int kAttnStages = 2;
 constexpr int kAttnCtasPerSm = 3;
 constexpr int kAttnChunk = 256;
+constexpr int kAttnMaxBatch = 1024;  // sequences per call (one counter each in the workspace)
 constexpr int kAttnConsumers = 128;
 constexpr int kAttnThreads = 32 + kAttnConsumers;
 constexpr float kNegBig = -1.0e30f;
@@ -140,7 +146,6 @@ struct alignas(128) AttnSmem {
   uint64_t full[kAttnStages];
   uint64_t empty[kAttnStages];
   int4 meta[kAttnStages];  // item (-1: no more work), stage in item, valid tokens, last stage of item
-  int last_bh;
   int last_row;
 };
 
@@ -156,11 +161,11 @@ struct AttnArgs {
   __half* out;
   int8_t* q_out;
   float* q_scale;
-  float* part_ml;    // [B*H*n_chunks][2]
-  float* part_acc;   // [B*H*n_chunks][D]
-  int32_t* cnt_bh;   // [B*H]
-  int32_t* cnt_row;  // [B]
-  int32_t* work;     // [2]: next item, CTAs done
+  float* part_ml;     // [B*H*n_chunks][2]
+  float* part_acc;    // [B*H*n_chunks][D]
+  uint32_t* flags;    // [B*H*n_chunks]: launch epoch + 1 once the chunk's partial is written
+  int32_t* cnt_row;   // [B]
+  int32_t* work;      // [3]: next item beyond the first grid.x, CTAs done, launch epoch
   int* status;
 };
 
@@ -192,6 +197,16 @@ __device__ __forceinline__ int atomic_add_acq_rel(int32_t* p, int v) {
   return old;
 }
 
+__device__ __forceinline__ void store_release(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t load_acquire(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
 __device__ __forceinline__ int attn_ctx(const AttnArgs& p, int b) {
   return min(max(0, p.ctx_lens[b]), p.max_blocks * p.block_size);
 }
@@ -206,9 +221,15 @@ __device__ __forceinline__ void unpack8(const uint4& x, float (&v)[8]) {
   }
 }
 
+// End of an item: the token streams are merged into the chunk's partial
+// (max, sum, acc[D]). A chunk other than the last one of (b, h) publishes its
+// partial and raises its flag (no round trip: the consumers go straight on).
+// The last chunk owns (b, h): it waits for the earlier chunks' flags (those
+// items were taken from the queue before it), merges their partials in chunk
+// order and writes out[b, h].
 template <int D>
 __device__ void attn_item_end(const AttnArgs& p, AttnSmem<D>& s, int ct, int stream, int sl, int b, int h, int chunk,
-                              float m, float l, const float (&acc)[8]) {
+                              uint32_t epoch, float m, float l, const float (&acc)[8]) {
   constexpr int S = AttnSmem<D>::kStreams;
   const int bh = b * p.H + h;
 #pragma unroll
@@ -218,80 +239,101 @@ __device__ void attn_item_end(const AttnArgs& p, AttnSmem<D>& s, int ct, int str
     s.l[stream] = l;
   }
   consumer_bar();
-  const size_t pidx = (size_t)bh * p.n_chunks + chunk;
+  float mm = kNegBig, ll = 0.f, aa = 0.f;
   if (ct < D) {
-    float mm = kNegBig;
 #pragma unroll
     for (int i = 0; i < S; ++i) mm = fmaxf(mm, s.m[i]);
-    float ll = 0.f, aa = 0.f;
 #pragma unroll
     for (int i = 0; i < S; ++i) {
       const float w = exp2f(s.m[i] - mm);
       ll += s.l[i] * w;
       aa += s.acc[i][ct] * w;
     }
-    __stcg(p.part_acc + pidx * D + ct, aa);
-    if (ct == 0) {
-      __stcg(p.part_ml + pidx * 2, mm);
-      __stcg(p.part_ml + pidx * 2 + 1, ll);
+  }
+  const int active = max(1, (attn_ctx(p, b) + kAttnChunk - 1) / kAttnChunk);
+  const size_t pbase = (size_t)bh * p.n_chunks;
+  if (chunk < active - 1) {
+    if (ct < D) {
+      __stcg(p.part_acc + (pbase + chunk) * D + ct, aa);
+      if (ct == 0) {
+        __stcg(p.part_ml + (pbase + chunk) * 2, mm);
+        __stcg(p.part_ml + (pbase + chunk) * 2 + 1, ll);
+      }
+    }
+    consumer_bar();  // every partial write is ordered before the flag (cumulative release)
+    if (ct == 0) store_release(p.flags + pbase + chunk, epoch + 1);
+    consumer_bar();  // stream state in shared memory is free for the next item
+    return;
+  }
+  if (ct == 0) {
+    for (int c = 0; c < active - 1; ++c) {
+      if ((int)(load_acquire(p.flags + pbase + c) - (epoch + 1)) >= 0) continue;
+      const uint64_t t0 = globaltimer_ns();
+      while ((int)(load_acquire(p.flags + pbase + c) - (epoch + 1)) < 0) {
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+          atomicCAS(p.status, 0, NPL_DEV_TIMEOUT_EPILOGUE);
+          break;
+        }
+      }
     }
   }
   consumer_bar();
-  const int active = max(1, (attn_ctx(p, b) + kAttnChunk - 1) / kAttnChunk);
-  if (ct == 0) s.last_bh = (atomic_add_acq_rel(p.cnt_bh + bh, 1) + 1 == active);
-  consumer_bar();
-  if (s.last_bh) {
-    if (ct < D) {
-      float mm = kNegBig;
-      for (int c = 0; c < active; ++c) mm = fmaxf(mm, __ldcg(p.part_ml + ((size_t)bh * p.n_chunks + c) * 2));
-      float ll = 0.f, aa = 0.f;
-      for (int c = 0; c < active; ++c) {
-        const size_t pi = (size_t)bh * p.n_chunks + c;
-        const float w = exp2f(__ldcg(p.part_ml + pi * 2) - mm);
-        ll += __ldcg(p.part_ml + pi * 2 + 1) * w;
-        aa += __ldcg(p.part_acc + pi * D + ct) * w;
-        __stcg(p.part_acc + pi * D + ct, 0.f);
+  if (ct < D) {
+    // chunk order, then this (last) chunk: the same result whatever the timing
+    float m2 = kNegBig, l2 = 0.f, a2 = 0.f;
+    for (int c = 0; c <= active - 1; ++c) {
+      float mc, lc, ac;
+      if (c < active - 1) {
+        mc = __ldcg(p.part_ml + (pbase + c) * 2);
+        lc = __ldcg(p.part_ml + (pbase + c) * 2 + 1);
+        ac = __ldcg(p.part_acc + (pbase + c) * D + ct);
+      } else {
+        mc = mm;
+        lc = ll;
+        ac = aa;
       }
-      p.out[(size_t)bh * D + ct] = __float2half_rn(ll > 0.f ? aa / ll : 0.f);
+      const float mn = fmaxf(m2, mc);
+      const float w0 = exp2f(m2 - mn), w1 = exp2f(mc - mn);
+      l2 = l2 * w0 + lc * w1;
+      a2 = a2 * w0 + ac * w1;
+      m2 = mn;
     }
-    consumer_bar();  // every merge read of part_ml is done before it is cleared
-    for (int i = ct; i < 2 * active; i += kAttnConsumers) __stcg(p.part_ml + (size_t)bh * p.n_chunks * 2 + i, 0.f);
-    if (ct == 0) p.cnt_bh[bh] = 0;
-    if (p.q_out) {
-      consumer_bar();
-      if (ct == 0) s.last_row = (atomic_add_acq_rel(p.cnt_row + b, 1) + 1 == p.H);
-      consumer_bar();
-      if (s.last_row) {
-        // per-token quantisation of the attention row of b (as npl_quant_rows)
-        const int n = p.H * D;
-        const __half* row = p.out + (size_t)b * n;
-        float amax = 0.f;
-        for (int i = ct * 8; i < n; i += kAttnConsumers * 8) {
-          float v[8];
-          unpack8(__ldcg(reinterpret_cast<const uint4*>(row + i)), v);
+    p.out[(size_t)bh * D + ct] = __float2half_rn(l2 > 0.f ? a2 / l2 : 0.f);
+  }
+  if (p.q_out) {
+    consumer_bar();  // out[b, h] written by every thread before the count
+    if (ct == 0) s.last_row = (atomic_add_acq_rel(p.cnt_row + b, 1) + 1 == p.H);
+    consumer_bar();
+    if (s.last_row) {
+      // per-token quantisation of the attention row of b (as npl_quant_rows)
+      const int n = p.H * D;
+      const __half* row = p.out + (size_t)b * n;
+      float amax = 0.f;
+      for (int i = ct * 8; i < n; i += kAttnConsumers * 8) {
+        float v[8];
+        unpack8(__ldcg(reinterpret_cast<const uint4*>(row + i)), v);
 #pragma unroll
-          for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(v[j]));
-        }
-        amax = warp_max(amax);
-        if ((ct & 31) == 0) s.red[ct >> 5] = amax;
-        consumer_bar();
-        amax = fmaxf(fmaxf(s.red[0], s.red[1]), fmaxf(s.red[2], s.red[3]));
-        const float sc = scale_from_absmax(amax);
-        int8_t* qrow = p.q_out + (size_t)b * n;
-        for (int i = ct * 8; i < n; i += kAttnConsumers * 8) {
-          float v[8];
-          unpack8(__ldcg(reinterpret_cast<const uint4*>(row + i)), v);
-          uint2 u;
-          uint32_t* w = reinterpret_cast<uint32_t*>(&u);
-          w[0] = w[1] = 0;
+        for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(v[j]));
+      }
+      amax = warp_max(amax);
+      if ((ct & 31) == 0) s.red[ct >> 5] = amax;
+      consumer_bar();
+      amax = fmaxf(fmaxf(s.red[0], s.red[1]), fmaxf(s.red[2], s.red[3]));
+      const float sc = scale_from_absmax(amax);
+      int8_t* qrow = p.q_out + (size_t)b * n;
+      for (int i = ct * 8; i < n; i += kAttnConsumers * 8) {
+        float v[8];
+        unpack8(__ldcg(reinterpret_cast<const uint4*>(row + i)), v);
+        uint2 u;
+        uint32_t* w = reinterpret_cast<uint32_t*>(&u);
+        w[0] = w[1] = 0;
 #pragma unroll
-          for (int j = 0; j < 8; ++j) w[j / 4] |= (uint32_t)(quantize_one(v[j], sc) & 0xff) << (8 * (j % 4));
-          *reinterpret_cast<uint2*>(qrow + i) = u;
-        }
-        if (ct == 0) {
-          p.q_scale[b] = sc;
-          p.cnt_row[b] = 0;
-        }
+        for (int j = 0; j < 8; ++j) w[j / 4] |= (uint32_t)(quantize_one(v[j], sc) & 0xff) << (8 * (j % 4));
+        *reinterpret_cast<uint2*>(qrow + i) = u;
+      }
+      if (ct == 0) {
+        p.q_scale[b] = sc;
+        p.cnt_row[b] = 0;
       }
     }
   }
@@ -333,9 +375,13 @@ __global__ void __launch_bounds__(kAttnThreads, kAttnCtasPerSm)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
+      // the first item of each CTA is blockIdx.x; the following ones come
+      // from the work counter (which counts items beyond the first grid.x)
+      int next = (int)blockIdx.x;
       while (ok) {
-        const int item = atomicAdd(p.work, 1);
+        const int item = next;
         if (item >= p.n_items) break;
+        next = (int)gridDim.x + atomicAdd(p.work, 1);
         const int chunk = item / bh_count, bh = item % bh_count;
         const int b = bh / p.H, h = bh % p.H, kvh = h / groups;
         const int ctx = attn_ctx(p, b);
@@ -389,11 +435,6 @@ __global__ void __launch_bounds__(kAttnThreads, kAttnCtasPerSm)
       if (ok && mbar_wait(&s.empty[stage], phase ^ 1, p.status, NPL_DEV_TIMEOUT_TMA)) {
         s.meta[stage] = make_int4(-1, 0, 0, 0);
         mbar_arrive(&s.full[stage]);
-        // the last CTA to run out of work resets the work counters
-        if (atomicAdd(p.work + 1, 1) + 1 == (int)gridDim.x) {
-          atomicExch(p.work, 0);
-          atomicExch(p.work + 1, 0);
-        }
       }
     }
   } else {
@@ -402,6 +443,7 @@ __global__ void __launch_bounds__(kAttnThreads, kAttnCtasPerSm)
     const int stream = ct / LPT, sl = ct % LPT;
     const unsigned gmask = LPT == 32 ? 0xffffffffu : (((1u << LPT) - 1) << ((ct & 31) & ~(LPT - 1)));
     const float qscale = p.scale * 1.4426950408889634f;  // scores in log2 units
+    const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(p.work + 2);
     float qv[8], acc[8];
     float m = kNegBig, l = 0.f;
     int stage = 0;
@@ -463,12 +505,20 @@ __global__ void __launch_bounds__(kAttnThreads, kAttnCtasPerSm)
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&s.empty[stage]);
-      if (meta.w) attn_item_end<D>(p, s, ct, stream, sl, b, h, chunk, m, l, acc);
+      if (meta.w) attn_item_end<D>(p, s, ct, stream, sl, b, h, chunk, epoch, m, l, acc);
       if (++stage == kAttnStages) {
         stage = 0;
         phase ^= 1;
       }
     }
+  }
+  // The last CTA to finish resets the work counters and advances the launch
+  // epoch for the next launch; every CTA has read the epoch by now.
+  __syncthreads();
+  if (threadIdx.x == 0 && atomic_add_acq_rel(p.work + 1, 1) + 1 == (int)gridDim.x) {
+    p.work[0] = 0;
+    p.work[1] = 0;
+    p.work[2] += 1;
   }
 }
 
@@ -495,8 +545,16 @@ int make_cache_map(CUtensorMap* map, const void* base, int num_blocks, int block
   return NPL_OK;
 }
 
+// Workspace. The words that persist from call to call sit at fixed offsets,
+// so that calls of any shape can share one workspace: the work counters and
+// launch epoch, one counter per sequence (zero between calls) and one flag
+// per (sequence, head, chunk) (stamped with the epoch of the launch that
+// wrote the chunk's partial; a stale flag always holds an older epoch). The
+// partials follow; their layout depends on the shape.
+constexpr size_t kAttnMaxParts = size_t(1) << 18;  // (sequence, head, chunk) per call
+
 struct AttnLayout {
-  size_t ml, acc, cnt_bh, cnt_row, work, total;
+  size_t work, cnt_row, flags, ml, acc, total;
 };
 
 AttnLayout attn_layout(int B, int H, int D, int max_blocks, int block_size) {
@@ -504,12 +562,12 @@ AttnLayout attn_layout(int B, int H, int D, int max_blocks, int block_size) {
   const size_t n_chunks = std::max<size_t>(1, ((size_t)max_blocks * block_size + kAttnChunk - 1) / kAttnChunk);
   const size_t parts = (size_t)B * H * n_chunks;
   AttnLayout l;
-  l.ml = 0;
+  l.work = 0;
+  l.cnt_row = 256;
+  l.flags = l.cnt_row + al((size_t)kAttnMaxBatch * sizeof(int32_t));
+  l.ml = l.flags + al(kAttnMaxParts * sizeof(uint32_t));
   l.acc = l.ml + al(parts * 2 * sizeof(float));
-  l.cnt_bh = l.acc + al(parts * D * sizeof(float));
-  l.cnt_row = l.cnt_bh + al((size_t)B * H * sizeof(int32_t));
-  l.work = l.cnt_row + al((size_t)B * sizeof(int32_t));
-  l.total = l.work + 256;
+  l.total = l.acc + al(parts * D * sizeof(float));
   return l;
 }
 
@@ -578,6 +636,11 @@ extern "C" int npl_paged_decode_attention(const void* q, int B, int H, int Hkv, 
   for (const void* p : std::initializer_list<const void*>{q, k_cache, v_cache, out, (const void*)q_out})
     if (p && !aligned16(p)) return fail(NPL_ERR_ARG, "npl_paged_decode_attention: pointers must be 16-byte aligned");
   if (B == 0) return NPL_OK;
+  if (B > kAttnMaxBatch)
+    return fail(NPL_ERR_UNSUPPORTED, "npl_paged_decode_attention: at most %d sequences per call", kAttnMaxBatch);
+  if ((size_t)B * H * std::max(1, (max_blocks * block_size + kAttnChunk - 1) / kAttnChunk) > kAttnMaxParts)
+    return fail(NPL_ERR_UNSUPPORTED, "npl_paged_decode_attention: more than %zu (sequence, head, %d-token chunk)",
+                kAttnMaxParts, kAttnChunk);
   const AttnLayout lay = attn_layout(B, H, D, max_blocks, block_size);
   if (!workspace || workspace_bytes < lay.total || !aligned16(workspace))
     return fail(NPL_ERR_ARG, "npl_paged_decode_attention: workspace of %zu bytes required", lay.total);
@@ -606,7 +669,7 @@ extern "C" int npl_paged_decode_attention(const void* q, int B, int H, int Hkv, 
   p.q_scale = q_scale;
   p.part_ml = reinterpret_cast<float*>(ws + lay.ml);
   p.part_acc = reinterpret_cast<float*>(ws + lay.acc);
-  p.cnt_bh = reinterpret_cast<int32_t*>(ws + lay.cnt_bh);
+  p.flags = reinterpret_cast<uint32_t*>(ws + lay.flags);
   p.cnt_row = reinterpret_cast<int32_t*>(ws + lay.cnt_row);
   p.work = reinterpret_cast<int32_t*>(ws + lay.work);
   p.status = device_status_ptr();
