@@ -237,9 +237,8 @@ int npl_rope_store_kv(const void* qkv, int ld_qkv, int T, int H, int Hkv, int D,
  * D is 64 or 128; block_size a multiple of 64, or 8, 16 or 32; B <= 1024 and
  * B * H * ceil(max_blocks * block_size / 256) <= 2^18. The workspace
  * (npl_decode_attention_workspace_bytes) must be zero-filled before its first
- * use and then passed to this function only: it keeps a launch counter and
- * per-chunk flags that hold the launch in which the chunk was written. Calls
- * of any shape may share it when they are ordered on one stream.
+ * use; every call leaves its counters and flags zero again, so calls of any
+ * shape may share it when they are ordered on one stream.
  */
 size_t npl_decode_attention_workspace_bytes(int B, int H, int D, int max_blocks, int block_size);
 int npl_paged_decode_attention(const void* q, int B, int H, int Hkv, int D, const void* k_cache,

@@ -117,8 +117,8 @@ __global__ void rope_store_kernel(const __half* __restrict__ qkv, int ld_qkv, in
 // many heads (adjacent 256-byte pieces of each 8 KB cache row), which keeps
 // the DRAM accesses local. At the end of an item the streams are merged into
 // a partial (max, sum, acc[D]); chunks before the last one of (b, h) publish
-// theirs behind a per-chunk flag that carries the launch epoch (the flags are
-// never reset), and the item of the last chunk merges them into out[b, h].
+// theirs behind a per-chunk flag, and the item of the last chunk (which waits
+// for the flags and clears them) merges them into out[b, h].
 // With q_out given, the CTA that completes the last head of b quantises the
 // attention row of b per token (w8a8.py:106-115), which is the input of the O
 // projection.
@@ -163,9 +163,9 @@ struct AttnArgs {
   float* q_scale;
   float* part_ml;     // [B*H*n_chunks][2]
   float* part_acc;    // [B*H*n_chunks][D]
-  uint32_t* flags;    // [B*H*n_chunks]: launch epoch + 1 once the chunk's partial is written
+  uint32_t* flags;    // [B*H*n_chunks]: 1 once the chunk's partial is written (cleared by its owner)
   int32_t* cnt_row;   // [B]
-  int32_t* work;      // [3]: next item beyond the first grid.x, CTAs done, launch epoch
+  int32_t* work;      // [2]: next item beyond the first grid.x, CTAs done
   int* status;
 };
 
@@ -229,7 +229,7 @@ __device__ __forceinline__ void unpack8(const uint4& x, float (&v)[8]) {
 // order and writes out[b, h].
 template <int D>
 __device__ void attn_item_end(const AttnArgs& p, AttnSmem<D>& s, int ct, int stream, int sl, int b, int h, int chunk,
-                              uint32_t epoch, float m, float l, const float (&acc)[8]) {
+                              float m, float l, const float (&acc)[8]) {
   constexpr int S = AttnSmem<D>::kStreams;
   const int bh = b * p.H + h;
 #pragma unroll
@@ -261,20 +261,24 @@ __device__ void attn_item_end(const AttnArgs& p, AttnSmem<D>& s, int ct, int str
       }
     }
     consumer_bar();  // every partial write is ordered before the flag (cumulative release)
-    if (ct == 0) store_release(p.flags + pbase + chunk, epoch + 1);
+    if (ct == 0) store_release(p.flags + pbase + chunk, 1u);
     consumer_bar();  // stream state in shared memory is free for the next item
     return;
   }
   if (ct == 0) {
+    // wait for the earlier chunks' flags and clear each one once seen: no
+    // later item of this launch sets it again, so flags are zero between calls
     for (int c = 0; c < active - 1; ++c) {
-      if ((int)(load_acquire(p.flags + pbase + c) - (epoch + 1)) >= 0) continue;
-      const uint64_t t0 = globaltimer_ns();
-      while ((int)(load_acquire(p.flags + pbase + c) - (epoch + 1)) < 0) {
-        if (globaltimer_ns() - t0 > kWaitLimitNs) {
-          atomicCAS(p.status, 0, NPL_DEV_TIMEOUT_EPILOGUE);
-          break;
+      if (load_acquire(p.flags + pbase + c) == 0u) {
+        const uint64_t t0 = globaltimer_ns();
+        while (load_acquire(p.flags + pbase + c) == 0u) {
+          if (globaltimer_ns() - t0 > kWaitLimitNs) {
+            atomicCAS(p.status, 0, NPL_DEV_TIMEOUT_EPILOGUE);
+            break;
+          }
         }
       }
+      p.flags[pbase + c] = 0u;
     }
   }
   consumer_bar();
@@ -435,6 +439,11 @@ __global__ void __launch_bounds__(kAttnThreads, kAttnCtasPerSm)
       if (ok && mbar_wait(&s.empty[stage], phase ^ 1, p.status, NPL_DEV_TIMEOUT_TMA)) {
         s.meta[stage] = make_int4(-1, 0, 0, 0);
         mbar_arrive(&s.full[stage]);
+        // the last CTA to run out of work resets the work counters
+        if (atomicAdd(p.work + 1, 1) + 1 == (int)gridDim.x) {
+          atomicExch(p.work, 0);
+          atomicExch(p.work + 1, 0);
+        }
       }
     }
   } else {
@@ -443,7 +452,6 @@ __global__ void __launch_bounds__(kAttnThreads, kAttnCtasPerSm)
     const int stream = ct / LPT, sl = ct % LPT;
     const unsigned gmask = LPT == 32 ? 0xffffffffu : (((1u << LPT) - 1) << ((ct & 31) & ~(LPT - 1)));
     const float qscale = p.scale * 1.4426950408889634f;  // scores in log2 units
-    const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(p.work + 2);
     float qv[8], acc[8];
     float m = kNegBig, l = 0.f;
     int stage = 0;
@@ -505,20 +513,12 @@ __global__ void __launch_bounds__(kAttnThreads, kAttnCtasPerSm)
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&s.empty[stage]);
-      if (meta.w) attn_item_end<D>(p, s, ct, stream, sl, b, h, chunk, epoch, m, l, acc);
+      if (meta.w) attn_item_end<D>(p, s, ct, stream, sl, b, h, chunk, m, l, acc);
       if (++stage == kAttnStages) {
         stage = 0;
         phase ^= 1;
       }
     }
-  }
-  // The last CTA to finish resets the work counters and advances the launch
-  // epoch for the next launch; every CTA has read the epoch by now.
-  __syncthreads();
-  if (threadIdx.x == 0 && atomic_add_acq_rel(p.work + 1, 1) + 1 == (int)gridDim.x) {
-    p.work[0] = 0;
-    p.work[1] = 0;
-    p.work[2] += 1;
   }
 }
 
@@ -545,12 +545,11 @@ int make_cache_map(CUtensorMap* map, const void* base, int num_blocks, int block
   return NPL_OK;
 }
 
-// Workspace. The words that persist from call to call sit at fixed offsets,
-// so that calls of any shape can share one workspace: the work counters and
-// launch epoch, one counter per sequence (zero between calls) and one flag
-// per (sequence, head, chunk) (stamped with the epoch of the launch that
-// wrote the chunk's partial; a stale flag always holds an older epoch). The
-// partials follow; their layout depends on the shape.
+// Workspace. The words that must be zero when a call starts sit at fixed
+// offsets, so that calls of any shape can share one workspace: the work
+// counters, one counter per sequence and one flag per (sequence, head,
+// chunk); every call leaves them zero. The partials follow; their layout
+// depends on the shape and they are always written before they are read.
 constexpr size_t kAttnMaxParts = size_t(1) << 18;  // (sequence, head, chunk) per call
 
 struct AttnLayout {

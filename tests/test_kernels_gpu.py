@@ -307,9 +307,10 @@ def test_decode_attention_vs_oracle(K, b, h, hkv, bs, ctx):
 
 
 def test_decode_attention_shared_workspace(K):
-    """Calls of different shapes share one workspace (its flags only ever
-    advance) and each stays within tolerance of the oracle, with the fused
-    per-token quantisation; repeated shapes give identical outputs."""
+    """Calls of different shapes share one workspace and each stays within
+    tolerance of the oracle, with the fused per-token quantisation; repeated
+    shapes give identical outputs; every call leaves the workspace's counters
+    and flags zero."""
     from nanopointllm_b200 import synthetic as S
     prev = {}
     for b, h, mb, ctx in ((8, 32, 6, 1087), (2, 4, 2, 20), (4, 8, 3, 500), (1, 2, 40, 9000), (8, 32, 6, 1087)):
@@ -331,6 +332,11 @@ def test_decode_attention_shared_workspace(K):
         if key in prev:
             assert torch.equal(prev[key], out)
         prev[key] = out
+        # the counters and flags at the front of the workspace (work counters,
+        # 1024 sequence counters, 2^18 chunk flags) are zero after every call
+        torch.cuda.synchronize()
+        ws = K.PA.decode_attention_workspace(K.dev, b, h, 128, mb, bs)
+        assert int(ws[:256 + 4096 + (4 << 18)].count_nonzero()) == 0
     K.lib.device_status()
 
 
