@@ -324,6 +324,7 @@ __device__ void attn_item_end(const AttnArgs& p, AttnSmem<D>& s, int ct, int str
       consumer_bar();
       amax = fmaxf(fmaxf(s.red[0], s.red[1]), fmaxf(s.red[2], s.red[3]));
       const float sc = scale_from_absmax(amax);
+      const float rsc = quant_recip(sc);
       int8_t* qrow = p.q_out + (size_t)b * n;
       for (int i = ct * 8; i < n; i += kAttnConsumers * 8) {
         float v[8];
@@ -332,7 +333,7 @@ __device__ void attn_item_end(const AttnArgs& p, AttnSmem<D>& s, int ct, int str
         uint32_t* w = reinterpret_cast<uint32_t*>(&u);
         w[0] = w[1] = 0;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) w[j / 4] |= (uint32_t)(quantize_one(v[j], sc) & 0xff) << (8 * (j % 4));
+        for (int j = 0; j < 8; ++j) w[j / 4] |= (uint32_t)(quantize_one(v[j], sc, rsc) & 0xff) << (8 * (j % 4));
         *reinterpret_cast<uint2*>(qrow + i) = u;
       }
       if (ct == 0) {

@@ -375,7 +375,8 @@ constexpr int kRowGroup = 2;   // rows reduced together in the RMSNorm statistic
 constexpr int kRowChunks = 4;  // 16-byte chunks per thread and row in flight
 
 template <int NT>
-__device__ void produce_activations(const LinearArgs& p, int8_t* xslot, float* s_scale, float* s_inv, double* red,
+__device__ void produce_activations(const LinearArgs& p, int8_t* xslot, float* s_scale, float* s_inv, float* s_recip,
+                                    double* red,
                                     int ct) {
   const int ew = ct >> 5, lane = ct & 31;
   if (p.x_mode == NPL_X_F16_RMSNORM) {
@@ -461,11 +462,15 @@ __device__ void produce_activations(const LinearArgs& p, int8_t* xslot, float* s
                               fmaxf((float)red[2 * kRowGroup + ct], (float)red[3 * kRowGroup + ct]));
         s_inv[m0 + ct] = rr[ct];
         s_scale[m0 + ct] = scale_from_absmax(a);
+        s_recip[m0 + ct] = quant_recip(s_scale[m0 + ct]);
       }
       epi_bar();
     }
   } else {
-    for (int m = ct; m < p.M; m += 128) s_scale[m] = scale_from_absmax(__int_as_float(p.x_absmax[m]));
+    for (int m = ct; m < p.M; m += 128) {
+      s_scale[m] = scale_from_absmax(__int_as_float(p.x_absmax[m]));
+      s_recip[m] = quant_recip(s_scale[m]);
+    }
     epi_bar();
   }
   // Token tile slots: stream-K keeps one per unit of the CTA (slot u holds
@@ -521,10 +526,10 @@ __device__ void produce_activations(const LinearArgs& p, int8_t* xslot, float* s
             v[i] = __half2float(__float2half_rn(__fmul_rn(w[i], y)));
           }
         }
-        const float sc = s_scale[r];
+        const float sc = s_scale[r], rsc = s_recip[r];
         uint32_t* w32 = reinterpret_cast<uint32_t*>(&packed);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) w32[i >> 2] |= (uint32_t)(quantize_one(v[i], sc) & 0xff) << (8 * (i & 3));
+        for (int i = 0; i < 16; ++i) w32[i >> 2] |= (uint32_t)(quantize_one(v[i], sc, rsc) & 0xff) << (8 * (i & 3));
       }
       // 128-byte swizzle: 16-byte chunk c of row r sits at chunk c ^ (r % 8)
       *reinterpret_cast<uint4*>(xslot + (size_t)u * NT * kBlockK + r * kBlockK + ((chunk ^ (r & 7)) << 4)) = packed;
@@ -548,6 +553,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   int8_t* xslot = reinterpret_cast<int8_t*>(base + p.off_x);
   float* s_scale = reinterpret_cast<float*>(base + p.off_f);
   float* s_inv = s_scale + NT;
+  float* s_recip = s_inv + NT;
   constexpr uint32_t kTmemCols = tmem_cols_for(NT);
   constexpr int kAccBufs = acc_bufs_for(NT);
   constexpr uint32_t kIdesc = idesc_i8(kTileN, NT);
@@ -710,7 +716,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int ct = threadIdx.x - 64;
     pdl_wait();
     if constexpr (kXF16) {
-      produce_activations<NT>(p, xslot, s_scale, s_inv, reinterpret_cast<double*>(s_inv + NT), ct);
+      produce_activations<NT>(p, xslot, s_scale, s_inv, s_recip, reinterpret_cast<double*>(s_recip + NT), ct);
       mbar_arrive(&c.xready);
       if (p.x_mode == NPL_X_F16_ABSMAX) {
         // x_absmax is consumed: the last CTA to have read it zeroes it for the
@@ -996,7 +1002,7 @@ int layout_linear(LinearArgs& p) {
   const size_t stage_bytes = (size_t)kTileN * kBlockK + (x_int8 ? (size_t)NT * kBlockK : 0);
   const size_t xslots = x_int8 ? 0 : (size_t)p.x_slots * NT * kBlockK;
   const size_t reds = (size_t)p.red_bufs * NT * kTileN * sizeof(int32_t);
-  const size_t tail = 2 * NT * sizeof(float) + 8 * sizeof(double);
+  const size_t tail = 3 * NT * sizeof(float) + 8 * sizeof(double);
   p.off_a = align1k(sizeof(LinearCtl));
   // Decode tiles (NT <= 64) keep the CTA near 110 KB when they can, so that
   // the next kernel's CTA fits beside it on an SM and starts its weight loads

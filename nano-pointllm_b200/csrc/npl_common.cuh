@@ -104,10 +104,27 @@ __device__ __forceinline__ float scale_from_absmax(float absmax) {
   return fmaxf(__half2float(__float2half_rn(raw)), kFp16Tiny);
 }
 
-// quantize_symmetric (w8a8.py:33-43): clamp(rint(v / s), -127, 127).
-__device__ __forceinline__ int quantize_one(float v, float s) {
-  const int q = __float2int_rn(__fdiv_rn(v, s));
-  return max(-127, min(127, q));
+// quantize_symmetric (w8a8.py:33-43): clamp(rint(v / s), -127, 127), with
+// v / s the correctly rounded fp32 quotient.
+//
+// The quotient comes from the reciprocal r = RN(1/s) (quant_recip, once per
+// row) by Markstein's FMA division step (P. Markstein, "Computation of
+// elementary functions on the IBM RISC System/6000 processor", IBM J. Res.
+// Dev. 34(1), 1990): q1 = RN(v r); e = v - q1 s, exact with an FMA;
+// q = RN(q1 + e r), which is RN(v / s) when v, s and e are normal numbers.
+// They are whenever the result can differ from 0: s >= 2^-14 is normal, and
+// |v / s| >= 1/2 makes |v| >= 2^-15 and |e| >= ulp(q1 s) / 2 >= 2^-40; for
+// |v / s| < 1/2 the rounded integer is 0 either way (q stays below 1/2 or
+// rounds to it, and rint(+-1/2) = 0). The scales are fp16 values, so the
+// pairs (fp16 v, scale) are checked exhaustively against IEEE division by
+// the tests, and fp32 v by sampling.
+__device__ __forceinline__ float quant_recip(float s) { return __frcp_rn(s); }
+
+__device__ __forceinline__ int quantize_one(float v, float s, float r) {
+  const float q1 = __fmul_rn(v, r);
+  const float e = __fmaf_rn(-q1, s, v);
+  const float q = __fmaf_rn(e, r, q1);
+  return max(-127, min(127, __float2int_rn(q)));
 }
 
 template <typename T>

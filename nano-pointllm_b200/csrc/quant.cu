@@ -75,6 +75,7 @@ __global__ void __launch_bounds__(kQuantThreads) quant_rows_kernel(const T* __re
   }
   amax = block_max(amax, red);
   const float s = scale_from_absmax(amax);
+  const float rs = quant_recip(s);
   if (threadIdx.x == 0) scale[blockIdx.x] = s;
   int8_t* qrow = q + (size_t)blockIdx.x * ldq;
   for (int c = threadIdx.x * V; c < cols; c += kQuantThreads * V) {
@@ -82,7 +83,7 @@ __global__ void __launch_bounds__(kQuantThreads) quant_rows_kernel(const T* __re
     Vec<T>::load(row + c, v);
     int qi[V];
 #pragma unroll
-    for (int i = 0; i < V; ++i) qi[i] = quantize_one(v[i], s);
+    for (int i = 0; i < V; ++i) qi[i] = quantize_one(v[i], s, rs);
     store_q<V>(qrow + c, qi);
   }
   pdl_trigger_after_writes();  // the rows may be weights, read by the next linear before its pdl_wait
@@ -147,6 +148,7 @@ __global__ void __launch_bounds__(kQuantThreads)
   }
   amax = block_max(amax, fred);
   const float s = scale_from_absmax(amax);
+  const float rs = quant_recip(s);
   if (threadIdx.x == 0) scale[blockIdx.x] = s;
 
   // 3. quantise (each thread re-reads only the chunks it wrote).
@@ -155,7 +157,7 @@ __global__ void __launch_bounds__(kQuantThreads)
     Vec<__half>::load(srow + c, v);
     int qi[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) qi[i] = quantize_one(v[i], s);
+    for (int i = 0; i < 8; ++i) qi[i] = quantize_one(v[i], s, rs);
     store_q<8>(q + base + c, qi);
   }
 }

@@ -49,6 +49,35 @@ def test_quant_rows_bit_exact(K, dtype, rows, cols):
     np.testing.assert_array_equal(cpu(s), so)
 
 
+def test_quant_rows_every_fp16_value(K):
+    """Every finite fp16 value v with |v| <= A, quantised with the scale of a
+    row whose absmax is A, for ~200 A across the fp16 range: the kernel's
+    quotient (reciprocal + one FMA correction step) rounds like the IEEE fp32
+    division of the reference, bit for bit."""
+    allh = np.arange(1 << 16, dtype=np.uint16).view(np.float16)
+    allh = allh[np.isfinite(allh)]
+    amaxes = np.unique(np.concatenate([
+        np.geomspace(6.2e-5, 65504, 160), [1.0, 127.0, 2.0 ** -14, 3e-5, 1e-7, 0.0],
+        np.random.default_rng(0).uniform(0.01, 100, 40)]).astype(np.float16))
+    width = (allh.size + 1 + 15) // 16 * 16  # every value + the row's absmax
+    rows = np.zeros((amaxes.size, width), dtype=np.float16)
+    for i, a in enumerate(amaxes):
+        v = allh[np.abs(allh.astype(np.float32)) <= np.float32(a)]
+        rows[i, :v.size] = v
+        rows[i, v.size] = a  # the row's absmax is exactly a
+    q, s = K.W.dynamic_per_token_quant(torch.from_numpy(rows).to(K.dev))
+    qo, so = O.dynamic_per_token_quant(rows)
+    np.testing.assert_array_equal(cpu(s), so)
+    np.testing.assert_array_equal(cpu(q), qo)
+    # fp32 inputs: sampled
+    g = torch.Generator().manual_seed(5)
+    x = torch.randn(64, 65536, generator=g) * torch.logspace(-6, 4, 64).reshape(-1, 1)
+    q, s = K.W.dynamic_per_token_quant(x.to(K.dev))
+    qo, so = O.dynamic_per_token_quant(x.numpy())
+    np.testing.assert_array_equal(cpu(s), so)
+    np.testing.assert_array_equal(cpu(q), qo)
+
+
 def test_quant_golden_small(K):
     g = golden("linear_small.npz")
     for tag in ("f32", "f16"):
