@@ -22,6 +22,16 @@ replays the graph and reads the 8 greedy tokens back to the host.
 With --gpus N (torchrun, one process per GPU) every rank runs an independent
 replica on its own requests (data parallel, no collective in the step).
 
+``--kernel-case NAME`` runs one op of the step alone (``--warmup`` eager
+launches, then ``--steps`` launches captured in a CUDA graph and replayed
+twice) on synthetic data of the config-3 / config-4 shapes and prints its
+per-launch device time and algorithmic throughput; it is the command the ncu
+summaries in profiles/ are taken with. Cases: qkv, o, gate_up,
+down, lm_head (decode linears, M = 8), attention (B = 8, context 1040),
+rmsnorm_quant, prefill (the five config-4 GEMMs at M = 4480), int8_peak
+(cuBLASLt int8 GEMM through torch._int_mm, 8192^3: the measured int8 tensor
+peak the prefill roofline is reported against).
+
 ``--impl reference`` times the reference's CPU W8A8 path on the host cores:
 the numpy port of the reference algorithm in oracle/ (the reference itself is
 Python/torch code that cannot run on the GPU box), on a bounded sample of the
@@ -166,7 +176,14 @@ def linear_bytes(m: int, n: int, k: int, out_cols: int, residual: bool, fp16_x: 
     return n * k + 4 * n + x + 2 * m * out_cols + (2 * m * out_cols if residual else 0)
 
 
-def op_bytes(shape, name: str, ctx_len: int, fused_mlp: bool = True) -> int:
+# DRAM bytes (read + write) per launch of the decode linears, from an ncu
+# capture on B200 of `bench.py --kernel-case <shape>` (dram__bytes_read.sum +
+# dram__bytes_write.sum, median of 3 launches, weights cold in L2).
+MEASURED_LINEAR_TRAFFIC = {"linear.qkv": 50_900_480, "linear.o": 16_980_480, "linear.gate_up": 91_805_696,
+                           "linear.down": 45_483_008, "linear.lm_head": 133_465_600}
+
+
+def op_bytes(shape, name: str, ctx_len: int, fused_mlp: bool = False) -> int:
     m, h, i_, v = BATCH, shape.hidden, shape.intermediate, shape.vocab
     qkv_n = (shape.heads + 2 * shape.kv_heads) * shape.head_dim
     if name == "linear.qkv":  # q out, k/v written to the cache (+ positions, slots, cos/sin rows)
@@ -317,6 +334,7 @@ def run_ours(args, torch, dist, rank: int, world: int, device) -> dict | None:
     lin_bytes = sum(op_bytes(shape, n, ctx_mid, fused) * len(per_op[n]) for n in lin_names)
     lin_launches = sum(len(per_op[n]) for n in lin_names)
     achieved = lin_bytes / (lin_ms * 1e-3) / 1e9
+    traffic = sum(MEASURED_LINEAR_TRAFFIC[n] * len(per_op[n]) for n in lin_names) / max(1, lin_launches)
     kernels = {}
     for name, times in per_op.items():
         b = op_bytes(shape, name, ctx_mid, fused)
@@ -348,7 +366,10 @@ def run_ours(args, torch, dist, rank: int, world: int, device) -> dict | None:
         "gpu_launches": launches_per_step * args.steps,
         "roofline": {"bound": "hbm", "kernel": "w8a8_linear_kernel (all 5 linears of the step)",
                      "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
-                     "frac": round(achieved / peak, 4), "traffic": None,
+                     "frac": round(achieved / peak, 4), "traffic": round(traffic),
+                     "traffic_unit": "DRAM bytes per launch (mean over the step's linear launches; ncu, "
+                                     "dram__bytes_read.sum + dram__bytes_write.sum)",
+                     "algorithmic_bytes_per_launch": round(lin_bytes / max(1, lin_launches)),
                      "algorithmic_bytes_per_step": lin_bytes // n_eager,
                      "launches_per_step": lin_launches // n_eager},
         "kernels": kernels,
@@ -419,6 +440,107 @@ def cpu_baseline(seconds: float = 20.0) -> dict:
             "s_per_step": round(step_s, 3)}
 
 
+# ------------------------------------------------------- single-op cases
+KERNEL_CASES = ("qkv", "o", "gate_up", "down", "lm_head", "attention", "rmsnorm_quant", "prefill", "int8_peak")
+
+
+def run_kernel_case(args, torch, device) -> dict:
+    from nanopointllm_b200 import _lib as L, paged_attention as PA, runner as R, synthetic as S, w8a8 as W
+    name = args.kernel_case
+    g = torch.Generator(device=device).manual_seed(0)
+    shape = S.LLAMA_7B
+    h, inter, v = shape.hidden, shape.intermediate, shape.vocab
+    qkv_n = (shape.heads + 2 * shape.kv_heads) * shape.head_dim
+
+    def timed(fn, n_launch):
+        """Device time per launch: the warm-up launches run eagerly, the timed
+        ones are replayed back to back from a CUDA graph (no host gaps)."""
+        for i in range(args.warmup):
+            fn(i)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for i in range(args.steps):
+                fn(i)
+        graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) * 1e3 / (args.steps * n_launch)
+
+    def weights(n, k):
+        # enough distinct weight copies that consecutive launches miss L2
+        copies = max(2, int(300e6 // (n * k)) + 1)
+        return [torch.randint(-127, 128, (n, k), dtype=torch.int8, device=device, generator=g) for _ in range(copies)]
+
+    line = {"case": name}
+    if name in ("qkv", "o", "gate_up", "down", "lm_head"):
+        n, k, epi, res = {"qkv": (qkv_n, h, L.EPI_NONE, False), "o": (h, h, L.EPI_RESIDUAL, True),
+                          "gate_up": (2 * inter, h, L.EPI_SILU_MUL, False),
+                          "down": (h, inter, L.EPI_RESIDUAL, True), "lm_head": (v, h, L.EPI_NONE, False)}[name]
+        ws = weights(n, k)
+        sw = torch.rand(n, device=device, generator=g) * 1e-3
+        qa = torch.randint(-127, 128, (BATCH, k), dtype=torch.int8, device=device, generator=g)
+        sa = torch.rand(BATCH, device=device, generator=g) * 1e-2
+        resid = torch.randn(BATCH, n, device=device, generator=g).half() if res else None
+        out = torch.empty(BATCH, n // 2 if epi == L.EPI_SILU_MUL else n, dtype=torch.float16, device=device)
+        us = timed(lambda i: W.linear_q(qa, sa, ws[i % len(ws)], sw, epilogue=epi, residual=resid, out=out), 1)
+        nbytes = op_bytes(shape, "linear." + name, CTX, False)
+        line.update({"kernel": "w8a8_linear_kernel", "shape": [BATCH, n, k], "us_per_launch": round(us, 2),
+                     "algorithmic_bytes": nbytes, "gbs": round(nbytes / us / 1e3, 1)})
+    elif name == "attention":
+        ctx_len, mb = CTX + 16, (CTX + 16 + BLOCK_SIZE - 1) // BLOCK_SIZE + 1
+        nb = BATCH * mb
+        sets = [(torch.randn(nb, BLOCK_SIZE, shape.kv_heads, shape.head_dim, device=device, generator=g).half(),
+                 torch.randn(nb, BLOCK_SIZE, shape.kv_heads, shape.head_dim, device=device, generator=g).half())
+                for _ in range(3)]
+        bt = S.permuted_block_tables(BATCH, mb, nb, seed=1).to(device)
+        q = torch.randn(BATCH, shape.heads, shape.head_dim, device=device, generator=g).half()
+        cl = torch.full((BATCH,), ctx_len, dtype=torch.int32, device=device)
+        q8 = torch.empty(BATCH, shape.heads * shape.head_dim, dtype=torch.int8, device=device)
+        qs = torch.empty(BATCH, dtype=torch.float32, device=device)
+        out = torch.empty_like(q)
+        us = timed(lambda i: PA.paged_decode_attention(q, sets[i % 3][0], sets[i % 3][1], bt, cl, shape.head_dim ** -0.5,
+                                                        1, out=out, quant_out=(q8, qs)), 1)
+        nbytes = op_bytes(shape, "attention", ctx_len)
+        line.update({"kernel": "decode_attn_kernel", "batch": BATCH, "context": ctx_len, "us_per_launch": round(us, 2),
+                     "algorithmic_bytes": nbytes, "gbs": round(nbytes / us / 1e3, 1)})
+    elif name == "rmsnorm_quant":
+        x = torch.randn(BATCH, h, device=device, generator=g).half()
+        w = torch.ones(h, device=device).half()
+        us = timed(lambda i: R.rmsnorm_quant(x, w, 1e-6), 1)
+        line.update({"kernel": "rmsnorm_quant_kernel", "shape": [BATCH, h], "us_per_launch": round(us, 2)})
+    elif name == "prefill":
+        m = 4480
+        gemms = [("qkv", qkv_n, h), ("o", h, h), ("gate_up", 2 * inter, h), ("down", h, inter), ("lm_head", v, h)]
+        xs = {k: torch.randint(-127, 128, (m, k), dtype=torch.int8, device=device, generator=g) for k in (h, inter)}
+        sa = torch.rand(m, device=device, generator=g) * 1e-2
+        wts = [(torch.randint(-127, 128, (n, k), dtype=torch.int8, device=device, generator=g),
+                torch.rand(n, device=device, generator=g) * 1e-3) for _, n, k in gemms]
+        outs = [torch.empty(m, n, dtype=torch.float16, device=device) for _, n, _ in gemms]
+
+        def all5(i):
+            for (nm, n, k), (qw, sw), o in zip(gemms, wts, outs):
+                W.linear_q(xs[k], sa, qw, sw, out=o)
+        us = timed(all5, len(gemms))
+        ops = sum(2 * m * n * k for _, n, k in gemms)
+        t_step = us * len(gemms)
+        line.update({"kernel": "w8a8_linear_kernel (NT = 256 tiles)", "config": "config4: M = 4480, the 5 GEMMs",
+                     "us_per_5_gemms": round(t_step, 1), "tops": round(ops / t_step / 1e6, 1), "ops": ops})
+    elif name == "int8_peak":
+        n = 8192
+        a = torch.randint(-127, 128, (n, n), dtype=torch.int8, device=device, generator=g)
+        b = torch.randint(-127, 128, (n, n), dtype=torch.int8, device=device, generator=g)
+        us = timed(lambda i: torch._int_mm(a, b), 1)
+        line.update({"kernel": "cuBLASLt int8 GEMM (torch._int_mm)", "shape": [n, n, n],
+                     "us_per_launch": round(us, 1), "tops": round(2 * n ** 3 / us / 1e6, 1)})
+    L.device_status()
+    return line
+
+
 def run_reference(args, rank: int) -> dict | None:
     if rank != 0:
         return None
@@ -448,6 +570,7 @@ def main() -> int:
     ap.add_argument("--layers", type=int, default=32, help="fewer layers only for quick checks (not the metric)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=20.0)
+    ap.add_argument("--kernel-case", choices=KERNEL_CASES, help="run one op alone (profiling harness)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -466,6 +589,9 @@ def main() -> int:
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
+    if args.kernel_case:
+        print(json.dumps(run_kernel_case(args, torch, device)))
+        return 0
     if world > 1:
         import datetime
         import torch.distributed as dist
