@@ -73,6 +73,32 @@ int npl_quant_rows(const void* x, int x_dtype, int rows, int cols, int ldx, int8
                    float* scale, void* stream);
 
 /*
+ * The two halves of npl_quant_rows, for a tensor-parallel layer whose input
+ * rows are split over ranks (the per-token scale needs the absmax of the
+ * whole row, a max over ranks; no counterpart in the reference, which runs on
+ * one device):
+ *   npl_row_absmax:        absmax_out[r] = max |x[r, :]| as fp32 bits (int32)
+ *   npl_quant_rows_absmax: scale and q as npl_quant_rows, from the given
+ *                          absmax_in[r] (fp32 bits) instead of the row's own
+ * Same shape and alignment rules as npl_quant_rows.
+ */
+int npl_row_absmax(const void* x, int x_dtype, int rows, int cols, int ldx, int32_t* absmax_out, void* stream);
+int npl_quant_rows_absmax(const void* x, int x_dtype, int rows, int cols, int ldx, const int32_t* absmax_in,
+                          int8_t* q, int ldq, float* scale, void* stream);
+
+/*
+ * Dequantisation of int32 accumulators, as the epilogue of npl_w8a8_linear
+ * (w8a8.py:118-139): v = ((acc[m, n] * sa[m]) * sw[n]) (+ bias[n]);
+ * NPL_EPI_NONE writes v as out_dtype, NPL_EPI_RESIDUAL writes
+ * fp16(fp16(v) + residual[m, n]). For a row-parallel linear whose int32
+ * partial accumulators were summed over ranks (no counterpart in the
+ * reference).
+ */
+int npl_dequant(const int32_t* acc, int ld_acc, const float* sa, const float* sw, const float* bias_or_null,
+                int M, int N, int epilogue, const void* residual_or_null, int ld_res, void* out, int ld_out,
+                int out_dtype, void* stream);
+
+/*
  * Fused RMSNorm + per-token int8 quantisation of fp16 rows (contiguous):
  *   s = residual ? fp16(x + residual) : x            (sum_out <- s if given)
  *   n = fp16(w * fp16(s * 1/sqrt(mean(s^2) + eps)))  (normed_out <- n if given)

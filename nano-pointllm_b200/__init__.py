@@ -12,10 +12,13 @@ Public surface, mirroring the reference ``nanopointllm`` API for this path:
   rope_store_kvcache
 * ``nanopointllm_b200.runner``          - W8A8 Llama decode runner
   (inject/quantize a model, prefill + decode steps, CUDA-graph decode)
+* ``nanopointllm_b200.tp``              - the same runner split over GPUs
+  (tensor parallel: column-parallel QKV / gate-up / LM head, row-parallel
+  O / down with int32 all-reduce)
 
 Every compute call goes through the C-ABI library ``libnpl_w8a8.so`` built
 from ``csrc/``; there is no CPU or library fallback.
 """
 from __future__ import annotations
 
-__all__ = ["w8a8", "paged_attention", "runner", "synthetic"]
+__all__ = ["w8a8", "paged_attention", "runner", "synthetic", "tp"]

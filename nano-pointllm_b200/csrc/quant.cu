@@ -3,6 +3,11 @@
 // npl_quant_rows     <- w8a8.py:33-50,106-115 (and :53-62 applied to weight rows)
 // npl_rmsnorm_quant  <- lightweight_runner.py:239-260 (eager RMSNorm / residual_norm)
 //                       followed by w8a8.py:106-115
+// npl_row_absmax, npl_quant_rows_absmax, npl_dequant
+//                    <- w8a8.py:106-115 and :118-139 split at the reductions a
+//                       tensor-parallel layer needs: the per-token absmax (max
+//                       over ranks) before quantising, and the int32
+//                       accumulator (sum over ranks) before dequantising
 //
 // One CTA per row; rows are short (decode: M <= 64 rows of 4096 or 11008), so
 // both kernels are latency-bound single passes over L2-resident data.
@@ -58,22 +63,36 @@ __device__ __forceinline__ void store_q<8>(int8_t* dst, const int (&q)[8]) {
   *reinterpret_cast<uint2*>(dst) = u;
 }
 
+// absmax_in (float bits, optional): use this per-row absmax instead of the
+// row's own; absmax_out (optional): record the row's absmax; q == null:
+// record the absmax only.
 template <typename T>
 __global__ void __launch_bounds__(kQuantThreads) quant_rows_kernel(const T* __restrict__ x, int cols, int ldx,
                                                                    int8_t* __restrict__ q, int ldq,
-                                                                   float* __restrict__ scale) {
+                                                                   float* __restrict__ scale,
+                                                                   const int32_t* __restrict__ absmax_in,
+                                                                   int32_t* __restrict__ absmax_out) {
   __shared__ float red[32];
   constexpr int V = Vec<T>::N;
   pdl_wait();
   const T* row = x + (size_t)blockIdx.x * ldx;
   float amax = 0.f;
-  for (int c = threadIdx.x * V; c < cols; c += kQuantThreads * V) {
-    float v[V];
-    Vec<T>::load(row + c, v);
+  if (absmax_in) {
+    amax = __int_as_float(absmax_in[blockIdx.x]);
+  } else {
+    for (int c = threadIdx.x * V; c < cols; c += kQuantThreads * V) {
+      float v[V];
+      Vec<T>::load(row + c, v);
 #pragma unroll
-    for (int i = 0; i < V; ++i) amax = fmaxf(amax, fabsf(v[i]));
+      for (int i = 0; i < V; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    }
+    amax = block_max(amax, red);
   }
-  amax = block_max(amax, red);
+  if (absmax_out && threadIdx.x == 0) absmax_out[blockIdx.x] = __float_as_int(amax);
+  if (!q) {
+    pdl_trigger();
+    return;
+  }
   const float s = scale_from_absmax(amax);
   const float rs = quant_recip(s);
   if (threadIdx.x == 0) scale[blockIdx.x] = s;
@@ -162,27 +181,98 @@ __global__ void __launch_bounds__(kQuantThreads)
   }
 }
 
+// out[m, n] = ((acc * sa[m]) * sw[n]) + bias[n], as the linear's epilogue
+// (NPL_EPI_NONE to out_dtype; NPL_EPI_RESIDUAL: fp16(fp16(v) + residual)).
+// Grid (M, ceil(N / 256)), one element per thread.
+__global__ void __launch_bounds__(256) dequant_kernel(const int32_t* __restrict__ acc, int ld_acc,
+                                                      const float* __restrict__ sa, const float* __restrict__ sw,
+                                                      const float* __restrict__ bias, int N, int epilogue,
+                                                      const __half* __restrict__ residual, int ld_res, void* out,
+                                                      int ld_out, int out_dtype) {
+  pdl_wait();
+  pdl_trigger();
+  const int m = blockIdx.x, n = blockIdx.y * 256 + threadIdx.x;
+  if (n >= N) return;
+  float v = __fmul_rn(__fmul_rn(__int2float_rn(acc[(size_t)m * ld_acc + n]), sa[m]), sw[n]);
+  if (bias) v = __fadd_rn(v, bias[n]);
+  if (epilogue == NPL_EPI_RESIDUAL) {
+    const float o = __half2float(__float2half_rn(v));
+    const float r = __half2float(residual[(size_t)m * ld_res + n]);
+    static_cast<__half*>(out)[(size_t)m * ld_out + n] = __float2half_rn(__fadd_rn(o, r));
+  } else if (out_dtype == NPL_F32) {
+    static_cast<float*>(out)[(size_t)m * ld_out + n] = v;
+  } else {
+    static_cast<__half*>(out)[(size_t)m * ld_out + n] = __float2half_rn(v);
+  }
+}
+
 }  // namespace
 }  // namespace npl
 
 using namespace npl;
 
-extern "C" int npl_quant_rows(const void* x, int x_dtype, int rows, int cols, int ldx, int8_t* q, int ldq,
-                              float* scale, void* stream) {
+namespace npl {
+namespace {
+
+int quant_rows_common(const char* what, const void* x, int x_dtype, int rows, int cols, int ldx,
+                      const int32_t* absmax_in, int32_t* absmax_out, int8_t* q, int ldq, float* scale,
+                      void* stream) {
   if (int rc = check_device()) return rc;
-  if (!x || !q || !scale) return fail(NPL_ERR_ARG, "npl_quant_rows: null pointer");
-  if (rows < 0 || cols <= 0 || cols % 16 || ldx < cols || ldx % 16 || ldq < cols || ldq % 16)
-    return fail(NPL_ERR_ARG, "npl_quant_rows: bad shape rows=%d cols=%d ldx=%d ldq=%d", rows, cols, ldx, ldq);
-  if (!aligned16(x) || !aligned16(q)) return fail(NPL_ERR_ARG, "npl_quant_rows: pointers must be 16-byte aligned");
+  if (!x || (q && !scale)) return fail(NPL_ERR_ARG, "%s: null pointer", what);
+  if (rows < 0 || cols <= 0 || cols % 16 || ldx < cols || ldx % 16 || (q && (ldq < cols || ldq % 16)))
+    return fail(NPL_ERR_ARG, "%s: bad shape rows=%d cols=%d ldx=%d ldq=%d", what, rows, cols, ldx, ldq);
+  if (!aligned16(x) || (q && !aligned16(q))) return fail(NPL_ERR_ARG, "%s: pointers must be 16-byte aligned", what);
   if (rows == 0) return NPL_OK;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (x_dtype == NPL_F32)
-    return launch_pdl("npl_quant_rows", quant_rows_kernel<float>, dim3(rows), dim3(kQuantThreads), 0, st,
-                      static_cast<const float*>(x), cols, ldx, q, ldq, scale);
+    return launch_pdl(what, quant_rows_kernel<float>, dim3(rows), dim3(kQuantThreads), 0, st,
+                      static_cast<const float*>(x), cols, ldx, q, ldq, scale, absmax_in, absmax_out);
   if (x_dtype == NPL_F16)
-    return launch_pdl("npl_quant_rows", quant_rows_kernel<__half>, dim3(rows), dim3(kQuantThreads), 0, st,
-                      static_cast<const __half*>(x), cols, ldx, q, ldq, scale);
-  return fail(NPL_ERR_ARG, "npl_quant_rows: x_dtype must be NPL_F32 or NPL_F16");
+    return launch_pdl(what, quant_rows_kernel<__half>, dim3(rows), dim3(kQuantThreads), 0, st,
+                      static_cast<const __half*>(x), cols, ldx, q, ldq, scale, absmax_in, absmax_out);
+  return fail(NPL_ERR_ARG, "%s: x_dtype must be NPL_F32 or NPL_F16", what);
+}
+
+}  // namespace
+}  // namespace npl
+
+extern "C" int npl_quant_rows(const void* x, int x_dtype, int rows, int cols, int ldx, int8_t* q, int ldq,
+                              float* scale, void* stream) {
+  if (!q) return fail(NPL_ERR_ARG, "npl_quant_rows: null pointer");
+  return quant_rows_common("npl_quant_rows", x, x_dtype, rows, cols, ldx, nullptr, nullptr, q, ldq, scale, stream);
+}
+
+extern "C" int npl_row_absmax(const void* x, int x_dtype, int rows, int cols, int ldx, int32_t* absmax_out,
+                              void* stream) {
+  if (!absmax_out) return fail(NPL_ERR_ARG, "npl_row_absmax: null pointer");
+  return quant_rows_common("npl_row_absmax", x, x_dtype, rows, cols, ldx, nullptr, absmax_out, nullptr, 0, nullptr,
+                           stream);
+}
+
+extern "C" int npl_quant_rows_absmax(const void* x, int x_dtype, int rows, int cols, int ldx,
+                                     const int32_t* absmax_in, int8_t* q, int ldq, float* scale, void* stream) {
+  if (!absmax_in || !q) return fail(NPL_ERR_ARG, "npl_quant_rows_absmax: null pointer");
+  return quant_rows_common("npl_quant_rows_absmax", x, x_dtype, rows, cols, ldx, absmax_in, nullptr, q, ldq, scale,
+                           stream);
+}
+
+extern "C" int npl_dequant(const int32_t* acc, int ld_acc, const float* sa, const float* sw, const float* bias,
+                           int M, int N, int epilogue, const void* residual, int ld_res, void* out, int ld_out,
+                           int out_dtype, void* stream) {
+  if (int rc = check_device()) return rc;
+  if (!acc || !sa || !sw || !out) return fail(NPL_ERR_ARG, "npl_dequant: null pointer");
+  if (M < 0 || N <= 0 || ld_acc < N || ld_out < N)
+    return fail(NPL_ERR_ARG, "npl_dequant: bad shape M=%d N=%d", M, N);
+  if (epilogue == NPL_EPI_RESIDUAL) {
+    if (!residual || ld_res < N || out_dtype != NPL_F16)
+      return fail(NPL_ERR_ARG, "npl_dequant: the residual epilogue needs an fp16 residual and fp16 out");
+  } else if (epilogue != NPL_EPI_NONE || (out_dtype != NPL_F16 && out_dtype != NPL_F32)) {
+    return fail(NPL_ERR_ARG, "npl_dequant: epilogue NPL_EPI_NONE (fp16/fp32 out) or NPL_EPI_RESIDUAL");
+  }
+  if (M == 0) return NPL_OK;
+  return launch_pdl("npl_dequant", dequant_kernel, dim3(M, (N + 255) / 256), dim3(256), 0,
+                    static_cast<cudaStream_t>(stream), acc, ld_acc, sa, sw, bias, N, epilogue,
+                    static_cast<const __half*>(residual), ld_res, out, ld_out, out_dtype);
 }
 
 extern "C" int npl_rmsnorm_quant(const void* x, const void* residual, const void* weight, float eps, int rows,

@@ -270,8 +270,11 @@ class W8A8LlamaRunner:
                                 device=h.device)
             h = h.index_select(0, last).contiguous()
         xq, xs, _ = self._op("rmsnorm_quant", rmsnorm_quant, h, self.norm, self.shape.eps)
-        logits = self._op("linear.lm_head", W.linear_q, xq, xs, self.lm_head.qweight, self.lm_head.wscale)
-        return logits.unsqueeze(0)
+        return self._lm_head(xq, xs).unsqueeze(0)
+
+    def _lm_head(self, xq: torch.Tensor, xs: torch.Tensor) -> torch.Tensor:
+        """int8 final-norm rows [T, hidden] + scales -> fp16 logits [T, vocab]."""
+        return self._op("linear.lm_head", W.linear_q, xq, xs, self.lm_head.qweight, self.lm_head.wscale)
 
     __call__ = forward
 

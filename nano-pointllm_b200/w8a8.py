@@ -68,6 +68,50 @@ def dynamic_per_token_quant(values: torch.Tensor, *, out: torch.Tensor | None = 
     return q.reshape(values.shape), s.reshape(*values.shape[:-1], 1)
 
 
+def row_absmax(values: torch.Tensor, *, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Per-row max |v| of [rows, K] (fp16/fp32) as fp32 bit patterns in int32
+    [rows] (non-negative floats order like their bits, so a MAX all-reduce of
+    these int32 values is the max of the floats)."""
+    _require_cuda(values)
+    x = _rows(values)
+    rows, k = x.shape
+    out = out if out is not None else torch.empty((rows,), dtype=torch.int32, device=x.device)
+    L.check(L.lib.npl_row_absmax(x.data_ptr(), _DT[x.dtype], rows, k, x.stride(0), out.data_ptr(),
+                                 L.stream_ptr(x.device)))
+    return out
+
+
+def quant_rows_absmax(values: torch.Tensor, absmax: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """dynamic_per_token_quant with the per-row absmax given (int32 fp32 bits,
+    e.g. reduced over the ranks that each hold part of the row): (q int8
+    [rows, K], scales fp32 [rows])."""
+    _require_cuda(values, absmax)
+    x = _rows(values)
+    rows, k = x.shape
+    q = torch.empty((rows, k), dtype=torch.int8, device=x.device)
+    s = torch.empty((rows,), dtype=torch.float32, device=x.device)
+    L.check(L.lib.npl_quant_rows_absmax(x.data_ptr(), _DT[x.dtype], rows, k, x.stride(0), absmax.data_ptr(),
+                                        q.data_ptr(), q.stride(0), s.data_ptr(), L.stream_ptr(x.device)))
+    return q, s
+
+
+def dequant(acc: torch.Tensor, sa: torch.Tensor, wscale: torch.Tensor, *, bias: torch.Tensor | None = None,
+            residual: torch.Tensor | None = None, out: torch.Tensor | None = None,
+            out_dtype: torch.dtype = torch.float16) -> torch.Tensor:
+    """int32 accumulators [M, N] -> ((acc * sa) * sw) + bias (+ residual in
+    fp16), as the linear's epilogue: the tail of a row-parallel linear after
+    its partial accumulators are summed over ranks."""
+    _require_cuda(acc, sa, wscale, bias, residual)
+    m, n = acc.shape
+    epi = L.EPI_RESIDUAL if residual is not None else L.EPI_NONE
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.float16 if residual is not None else out_dtype, device=acc.device)
+    L.check(L.lib.npl_dequant(acc.data_ptr(), acc.stride(0), sa.data_ptr(), wscale.data_ptr(), L.ptr(bias), m, n,
+                              epi, L.ptr(residual), 0 if residual is None else residual.stride(0), out.data_ptr(),
+                              out.stride(0), _DT[out.dtype], L.stream_ptr(acc.device)))
+    return out
+
+
 def per_output_weight_quant(weight: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     """w8a8.py:53-62 (per_output_weight_qdq): (qweight int8 [N, K], scales fp32 [N])."""
     if weight.dim() < 2:

@@ -1,0 +1,79 @@
+"""Tensor-parallel runner on 2 GPUs (NCCL, one process per GPU): prefill and
+greedy decode of the tiny Llama, eager and CUDA graph, bit-identical to the
+single-GPU W8A8LlamaRunner on the same weights (skipped with fewer than two
+GPUs)."""
+from __future__ import annotations
+
+import datetime
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank: int, world: int, port: int, errors) -> None:
+    import torch.distributed as dist
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+        import conftest  # noqa: F401  (registers the package)
+        from test_runner_gpu import _generate
+        from nanopointllm_b200 import runner as R, synthetic as S, tp as TP, _lib
+        shape = S.TINY
+        sd = S.llama_weights(shape, seed=0)
+        lengths = [37, 5, 64, 19]
+        prompts = S.decode_prompts(len(lengths), shape.vocab, lengths, seed=2)
+        bs, per_seq = 16, 6
+        bt = S.permuted_block_tables(len(lengths), per_seq, len(lengths) * per_seq, seed=3).numpy()
+        full = R.W8A8LlamaRunner(shape, sd, device=dev, num_blocks=len(lengths) * per_seq, block_size=bs)
+        t_ref, l_ref = _generate(full, prompts, bt, 5, dev)
+        for graph in (False, True):
+            run = TP.W8A8TPLlamaRunner(shape, sd, device=dev, num_blocks=len(lengths) * per_seq, block_size=bs)
+            t_tp, l_tp = _generate(run, prompts, bt, 5, dev, graph=graph)
+            np.testing.assert_array_equal(t_tp, t_ref)
+            np.testing.assert_array_equal(l_tp, l_ref)
+            del run
+        _lib.device_status()
+        torch.cuda.synchronize()
+        dist.barrier()
+        dist.destroy_process_group()
+    except BaseException as e:  # reported by the parent
+        import traceback
+        errors.put(f"rank {rank}: {e!r}\n{traceback.format_exc()}")
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_tp2_bit_identical_to_single_gpu():
+    import torch.multiprocessing as mp
+    world = 2
+    ctx = mp.get_context("spawn")
+    errors = ctx.SimpleQueue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, errors)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=400)
+    alive = [p for p in procs if p.is_alive()]
+    for p in alive:
+        p.kill()
+    msgs = []
+    while not errors.empty():
+        msgs.append(errors.get())
+    assert not alive, "a rank did not finish"
+    assert not msgs, "\n".join(msgs)
+    assert all(p.exitcode == 0 for p in procs)
