@@ -168,6 +168,22 @@ def step_metadata(torch, bt, step: int, device):
     return positions, slots, ctx
 
 
+# ------------------------------------------------------------- multi-rank
+def rank_seed(rank: int) -> int:
+    """Each data-parallel replica serves its own synthetic requests."""
+    return 1000 * rank
+
+
+def max_over_ranks(torch, dist, value: float, device) -> float:
+    """A time measured on every rank -> the slowest rank's (the whole job is
+    done when the last replica is done). Identity without a process group."""
+    if dist is None:
+        return value
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
 def linear_bytes(m: int, n: int, k: int, out_cols: int, residual: bool, fp16_x: bool) -> int:
     """Algorithmic bytes of one W8A8 linear launch: int8 weight + fp32 weight
     scales + activations (int8 + fp32 scales, or fp16 rows when the
@@ -208,8 +224,8 @@ def run_ours(args, torch, dist, rank: int, world: int, device) -> dict | None:
     shape = S.LLAMA_7B if args.layers == 32 else S.LlamaShape(**{**S.LLAMA_7B.as_dict(), "layers": args.layers})
     n_eager = 2
     steps_total = args.warmup + args.steps * 2 + n_eager + 2
-    run, bt = build_runner(torch, shape, steps_total, device, seed=1000 * rank)
-    first = prefill(torch, run, bt, device, seed=1000 * rank)
+    run, bt = build_runner(torch, shape, steps_total, device, seed=rank_seed(rank))
+    first = prefill(torch, run, bt, device, seed=rank_seed(rank))
     torch.cuda.synchronize()
 
     graph = R.DecodeGraph(run, BATCH, bt.shape[1])
@@ -250,11 +266,8 @@ def run_ours(args, torch, dist, rank: int, world: int, device) -> dict | None:
     e1.record(stream)
     torch.cuda.synchronize()
     clock_info = clocks.stop()
-    dev_ms = e0.elapsed_time(e1)
+    dev_ms = max_over_ranks(torch, dist, e0.elapsed_time(e1), device)
     if dist is not None:
-        t = torch.tensor([dev_ms], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        dev_ms = float(t.item())
         dist.barrier()
 
     # ---- e2e: host metadata in (pinned), graph replay, tokens out to host
@@ -281,12 +294,8 @@ def run_ours(args, torch, dist, rank: int, world: int, device) -> dict | None:
         d2h = host_out.numel() * host_out.element_size()
     e3.record(stream)
     torch.cuda.synchronize()
-    e2e_ms = e2.elapsed_time(e3)
+    e2e_ms = max_over_ranks(torch, dist, e2.elapsed_time(e3), device)
     step += args.steps
-    if dist is not None:
-        t = torch.tensor([e2e_ms], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
 
     # ---- per-kernel device time: a second decode graph whose ops are each
     # bracketed by timing events recorded inside the graph (on the launch
