@@ -334,9 +334,12 @@ def run_ours(args, torch, dist, rank: int, world: int, device) -> dict | None:
     del pgraph
     _lib.device_status()
 
+    standalone = standalone_linears(torch, run, shape, device) if rank == 0 else {}
     if rank != 0:
         return None
     peak, peak_kind = _peaks()
+    for v in standalone.values():
+        v["frac"] = round(v["gbs"] / peak, 4)
     lin_names = [n for n in per_op if n.startswith("linear.")]
     lin_ms = sum(sum(per_op[n]) for n in lin_names)
     fused = run.fuse_mlp_quant
@@ -380,13 +383,56 @@ def run_ours(args, torch, dist, rank: int, world: int, device) -> dict | None:
                                      "dram__bytes_read.sum + dram__bytes_write.sum)",
                      "algorithmic_bytes_per_launch": round(lin_bytes / max(1, lin_launches)),
                      "algorithmic_bytes_per_step": lin_bytes // n_eager,
-                     "launches_per_step": lin_launches // n_eager},
+                     "launches_per_step": lin_launches // n_eager,
+                     "timing": "each op bracketed by CUDA events recorded inside a copy of the decode graph "
+                               "(the events also stop the next kernel from starting early)",
+                     "standalone": standalone},
         "kernels": kernels,
         "clocks": clock_info,
     }
     if not args.no_cpu_baseline and world == 1:
         line["cpu_baseline"] = cpu_baseline(seconds=args.cpu_seconds)
     return line
+
+
+def standalone_linears(torch, run, shape, device) -> dict:
+    """Device time per launch of each decode linear over the step's own
+    weights: one CUDA graph of the 32 layers' launches of that projection
+    back to back (every weight read from DRAM), the activations fixed."""
+    from nanopointllm_b200 import _lib as L, w8a8 as W
+    g = torch.Generator(device=device).manual_seed(5)
+    out = {}
+    for name, attr, k, epi in (("linear.qkv", "qkv", shape.hidden, L.EPI_NONE),
+                               ("linear.o", "o", shape.heads * shape.head_dim, L.EPI_RESIDUAL),
+                               ("linear.gate_up", "gate_up", shape.hidden, L.EPI_SILU_MUL),
+                               ("linear.down", "down", shape.intermediate, L.EPI_RESIDUAL)):
+        lins = [getattr(layer, attr) for layer in run.layers]
+        n = lins[0].out_features
+        qa = torch.randint(-127, 128, (BATCH, k), dtype=torch.int8, device=device, generator=g)
+        sa = torch.rand(BATCH, device=device, generator=g) * 1e-2
+        res = torch.randn(BATCH, n, device=device, generator=g).half() if epi == L.EPI_RESIDUAL else None
+        dst = torch.empty(BATCH, n // 2 if epi == L.EPI_SILU_MUL else n, dtype=torch.float16, device=device)
+
+        def launches():
+            for lin in lins:
+                W.linear_q(qa, sa, lin.qweight, lin.wscale, epilogue=epi, residual=res, out=dst)
+        launches()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            launches()
+        graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / len(lins)
+        nbytes = op_bytes(shape, name, CTX, False)
+        out[name] = {"us_per_launch": round(us, 2), "gbs": round(nbytes / us / 1e3, 1)}
+        del graph
+    return out
 
 
 # ------------------------------------------------------------- CPU arm
