@@ -30,7 +30,9 @@ summaries in profiles/ are taken with. Cases: qkv, o, gate_up,
 down, lm_head (decode linears, M = 8), attention (B = 8, context 1040),
 rmsnorm_quant, prefill (the five config-4 GEMMs at M = 4480), int8_peak
 (cuBLASLt int8 GEMM through torch._int_mm, 8192^3: the measured int8 tensor
-peak the prefill roofline is reported against).
+peak the prefill roofline is reported against), package_load (start-up of
+a 7B-geometry runner with ``--layers`` layers from fp16 host weights against
+from the checksummed int8 package).
 
 ``--impl reference`` times the reference's CPU W8A8 path on the host cores:
 the numpy port of the reference algorithm in oracle/ (the reference itself is
@@ -496,7 +498,8 @@ def cpu_baseline(seconds: float = 20.0) -> dict:
 
 
 # ------------------------------------------------------- single-op cases
-KERNEL_CASES = ("qkv", "o", "gate_up", "down", "lm_head", "attention", "rmsnorm_quant", "prefill", "int8_peak")
+KERNEL_CASES = ("qkv", "o", "gate_up", "down", "lm_head", "attention", "rmsnorm_quant", "prefill", "int8_peak",
+                "package_load")
 
 
 def run_kernel_case(args, torch, device) -> dict:
@@ -592,8 +595,53 @@ def run_kernel_case(args, torch, device) -> dict:
         us = timed(lambda i: torch._int_mm(a, b), 1)
         line.update({"kernel": "cuBLASLt int8 GEMM (torch._int_mm)", "shape": [n, n, n],
                      "us_per_launch": round(us, 1), "tops": round(2 * n ** 3 / us / 1e6, 1)})
+    elif name == "package_load":
+        line.update(package_load_case(args, torch, device))
     L.device_status()
     return line
+
+
+def package_load_case(args, torch, device) -> dict:
+    """Start-up cost of a 7B-geometry runner (``--layers`` decoder layers):
+    built from fp16 host weights (H2D of the fp16 bytes + per-output
+    quantisation on the GPU, what a start without an int8 cache does) against
+    built from the checksummed int8 package (read + SHA-256 of every file on
+    the host thread pool + H2D of the int8 bytes). The package is written to
+    a temporary directory first, so its files are in the page cache: the
+    figure excludes the storage read."""
+    import tempfile
+    from dataclasses import replace
+    from nanopointllm_b200 import package as P, runner as R, synthetic as S
+    shape = replace(S.LLAMA_7B, layers=args.layers)
+    lazy = S.LazyLlamaWeights(shape, seed=0, device=str(device))
+    host = {name: lazy[name].cpu() for name in lazy.keys()}
+    fp16_bytes = sum(t.numel() * 2 for t in host.values())
+
+    def build(fn):
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        run = fn()
+        torch.cuda.synchronize()
+        dt = time.perf_counter() - t0
+        del run
+        torch.cuda.empty_cache()
+        return dt
+
+    with tempfile.TemporaryDirectory(prefix="npl_pkg_") as d:
+        t0 = time.perf_counter()
+        manifest = P.write_w8a8_llama_package(d, shape, host, device=device)
+        t_write = time.perf_counter() - t0
+        pkg_bytes = sum(int(e["bytes"]) for e in manifest["tensors"].values())
+        t_float, t_pkg = [], []
+        for _ in range(max(1, args.steps)):
+            t_float.append(build(lambda: R.W8A8LlamaRunner(shape, host, device=device, num_blocks=1, block_size=256)))
+            t_pkg.append(build(lambda: R.W8A8LlamaRunner.from_package(d, device=device, num_blocks=1,
+                                                                      block_size=256)))
+    tf, tp = statistics.median(t_float), statistics.median(t_pkg)
+    return {"layers": shape.layers, "package_gb": round(pkg_bytes / 1e9, 3), "fp16_gb": round(fp16_bytes / 1e9, 3),
+            "write_s": round(t_write, 2), "build_from_fp16_s": round(tf, 3), "build_from_package_s": round(tp, 3),
+            "package_gbs": round(pkg_bytes / tp / 1e9, 2), "speedup": round(tf / tp, 2),
+            "host_threads": os.cpu_count(), "note": "package files in the page cache (written just before)"}
 
 
 def run_reference(args, rank: int) -> dict | None:

@@ -43,6 +43,7 @@ import torch
 import torch.nn.functional as F
 
 from . import _lib as L
+from . import package as P
 from . import paged_attention as PA
 from . import w8a8 as W
 from .rope import rope_tables
@@ -92,22 +93,21 @@ def rmsnorm_quant(x: torch.Tensor, weight: torch.Tensor, eps: float, residual: t
 
 
 class W8A8Layer:
-    def __init__(self, shape: LlamaShape, sd: dict[str, torch.Tensor], idx: int, device: torch.device,
+    def __init__(self, shape: LlamaShape, src, idx: int, device: torch.device,
                  k_cache: torch.Tensor, v_cache: torch.Tensor):
+        """``src``: a weight source (package.FloatLlamaWeights or
+        package.PackagedLlamaWeights) giving each Linear's int8 weight and
+        per-output scales and the fp16 norm weights."""
         p = f"model.layers.{idx}."
-
-        def w(name):
-            return sd[p + name].to(device=device, dtype=torch.float16)
-
-        qkv = torch.cat([w("self_attn.q_proj.weight"), w("self_attn.k_proj.weight"), w("self_attn.v_proj.weight")])
-        self.qkv = W.W8A8Linear.from_float(qkv)
-        self.o = W.W8A8Linear.from_float(w("self_attn.o_proj.weight"))
-        gq, gs = W.per_output_weight_quant(w("mlp.gate_proj.weight"))
-        uq, us = W.per_output_weight_quant(w("mlp.up_proj.weight"))
+        qkv = [src.linear(p + "self_attn." + n) for n in ("q_proj", "k_proj", "v_proj")]
+        self.qkv = W.W8A8Linear(torch.cat([q for q, _ in qkv]), torch.cat([s for _, s in qkv]))
+        self.o = W.W8A8Linear(*src.linear(p + "self_attn.o_proj"))
+        gq, gs = src.linear(p + "mlp.gate_proj")
+        uq, us = src.linear(p + "mlp.up_proj")
         self.gate_up = W.W8A8Linear(W.pack_gate_up(gq, uq), W.pack_gate_up(gs, us))
-        self.down = W.W8A8Linear.from_float(w("mlp.down_proj.weight"))
-        self.input_norm = w("input_layernorm.weight").contiguous()
-        self.post_norm = w("post_attention_layernorm.weight").contiguous()
+        self.down = W.W8A8Linear(*src.linear(p + "mlp.down_proj"))
+        self.input_norm = src.dense(p + "input_layernorm.weight")
+        self.post_norm = src.dense(p + "post_attention_layernorm.weight")
         self.k_cache = k_cache
         self.v_cache = v_cache
 
@@ -118,6 +118,10 @@ class W8A8LlamaRunner:
     ``forward(input_ids | inputs_embeds, position_ids)`` reads the paged
     metadata from the thread-local ForwardContext and returns fp16 logits
     [1, T, vocab] (or only each sequence's last row with ``last_only=True``).
+
+    ``state_dict``: HF-named float weights (each Linear is quantised per
+    output channel on the GPU as its layer is built) or a weight source with
+    linear()/dense(), e.g. a checksummed int8 package (see from_package).
     """
 
     def __init__(self, shape: LlamaShape, state_dict: dict[str, torch.Tensor], *, device: torch.device,
@@ -140,13 +144,27 @@ class W8A8LlamaRunner:
         self.kv_pool = kv_pool
         self.block_size = kv_pool.shape[3]
         self.num_blocks = kv_pool.shape[2]
-        self.embed = state_dict["model.embed_tokens.weight"].to(device=self.device, dtype=torch.float16)
-        self.layers = [W8A8Layer(shape, state_dict, i, self.device, kv_pool[0, i], kv_pool[1, i])
+        src = P.as_weight_source(state_dict, self.device)
+        self.embed = src.dense("model.embed_tokens.weight")
+        self.layers = [W8A8Layer(shape, src, i, self.device, kv_pool[0, i], kv_pool[1, i])
                        for i in range(shape.layers)]
-        self.norm = state_dict["model.norm.weight"].to(device=self.device, dtype=torch.float16).contiguous()
-        self.lm_head = W.W8A8Linear.from_float(state_dict["lm_head.weight"].to(self.device, torch.float16))
+        self.norm = src.dense("model.norm.weight")
+        self.lm_head = W.W8A8Linear(*src.linear("lm_head"))
         self.cos, self.sin = rope_tables(shape.head_dim, shape.max_position, shape.rope_theta, self.device)
         self.scale = shape.head_dim ** -0.5
+
+    @classmethod
+    def from_package(cls, directory, *, device: torch.device, **kwargs):
+        """Builds the runner from a whole-model int8 package
+        (package.write_w8a8_llama_package) instead of float weights: no
+        weight is re-quantised, and every tensor is SHA-256-checked before it
+        reaches the GPU. kwargs as the constructor's (kv_pool, num_blocks,
+        block_size, ...)."""
+        src = P.PackagedLlamaWeights(directory, device)
+        try:
+            return cls(src.shape, src, device=device, **kwargs)
+        finally:
+            src.close()
 
     @classmethod
     def from_hf(cls, hf_model, kv_pool: torch.Tensor, device: torch.device | None = None) -> "W8A8LlamaRunner":

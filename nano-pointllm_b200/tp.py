@@ -31,6 +31,7 @@ import torch
 import torch.distributed as dist
 
 from . import _lib as L
+from . import package as P
 from . import paged_attention as PA
 from . import w8a8 as W
 from .rope import rope_tables
@@ -99,30 +100,29 @@ ZERO_ROW_SCALE = 2.0 ** -14
 
 
 class W8A8TPLayer:
-    def __init__(self, shape: LlamaShape, plan: TPPlan, sd: dict[str, torch.Tensor], idx: int, device: torch.device,
+    def __init__(self, shape: LlamaShape, plan: TPPlan, src, idx: int, device: torch.device,
                  k_cache: torch.Tensor, v_cache: torch.Tensor):
+        """``src`` gives the FULL int8 weights and per-row scales (quantised
+        from float weights, or read from a package); this rank keeps its
+        slices."""
         p = f"model.layers.{idx}."
-
-        def w(name):
-            return sd[p + name].to(device=device, dtype=torch.float16)
-
-        qkv_q, qkv_s = W.per_output_weight_quant(
-            torch.cat([w("self_attn.q_proj.weight"), w("self_attn.k_proj.weight"), w("self_attn.v_proj.weight")]))
+        qkv = [src.linear(p + "self_attn." + n) for n in ("q_proj", "k_proj", "v_proj")]
+        qkv_q, qkv_s = torch.cat([q for q, _ in qkv]), torch.cat([s for _, s in qkv])
         rows = qkv_rows(shape, plan).to(device)
         self.qkv = W.W8A8Linear(qkv_q[rows], qkv_s[rows])
         d = shape.head_dim
-        oq, os_ = W.per_output_weight_quant(w("self_attn.o_proj.weight"))
+        oq, os_ = src.linear(p + "self_attn.o_proj")
         self.o = W.W8A8Linear(oq[:, plan.h0 * d:(plan.h0 + plan.hl) * d], os_)
-        gq, gs = W.per_output_weight_quant(w("mlp.gate_proj.weight"))
-        uq, us = W.per_output_weight_quant(w("mlp.up_proj.weight"))
+        gq, gs = src.linear(p + "mlp.gate_proj")
+        uq, us = src.linear(p + "mlp.up_proj")
         sl = slice(plan.i0, plan.i1)
         self.gate_up = W.W8A8Linear(
             W.pack_gate_up(pad_rows(gq[sl], plan.il_pad), pad_rows(uq[sl], plan.il_pad)),
             W.pack_gate_up(pad_rows(gs[sl], plan.il_pad, ZERO_ROW_SCALE), pad_rows(us[sl], plan.il_pad, ZERO_ROW_SCALE)))
-        dq, ds = W.per_output_weight_quant(w("mlp.down_proj.weight"))
+        dq, ds = src.linear(p + "mlp.down_proj")
         self.down = W.W8A8Linear(pad_cols(dq[:, sl], plan.il_pad), ds)
-        self.input_norm = w("input_layernorm.weight").contiguous()
-        self.post_norm = w("post_attention_layernorm.weight").contiguous()
+        self.input_norm = src.dense(p + "input_layernorm.weight")
+        self.post_norm = src.dense(p + "post_attention_layernorm.weight")
         self.k_cache = k_cache
         self.v_cache = v_cache
 
@@ -152,11 +152,12 @@ class W8A8TPLlamaRunner(W8A8LlamaRunner):
         self.kv_pool = kv_pool
         self.block_size = kv_pool.shape[3]
         self.num_blocks = kv_pool.shape[2]
-        self.embed = state_dict["model.embed_tokens.weight"].to(device=self.device, dtype=torch.float16)
-        self.layers = [W8A8TPLayer(shape, self.plan, state_dict, i, self.device, kv_pool[0, i], kv_pool[1, i])
+        src = P.as_weight_source(state_dict, self.device)
+        self.embed = src.dense("model.embed_tokens.weight")
+        self.layers = [W8A8TPLayer(shape, self.plan, src, i, self.device, kv_pool[0, i], kv_pool[1, i])
                        for i in range(shape.layers)]
-        self.norm = state_dict["model.norm.weight"].to(device=self.device, dtype=torch.float16).contiguous()
-        hq, hs = W.per_output_weight_quant(state_dict["lm_head.weight"].to(self.device, torch.float16))
+        self.norm = src.dense("model.norm.weight")
+        hq, hs = src.linear("lm_head")
         vs = slice(self.plan.v0, self.plan.v1)
         self.lm_head = W.W8A8Linear(pad_rows(hq[vs], self.plan.vl_pad), pad_rows(hs[vs], self.plan.vl_pad,
                                                                                  ZERO_ROW_SCALE))

@@ -17,6 +17,9 @@ Reference entry points used (paths relative to the reference root):
   nanopointllm/llama/paged_attention.py     store_kvcache, _paged_decode_attention_pytorch
   nanopointllm/llama/inject_paged.py        inject_paged_attention
   nanopointllm/engine/kv_pool.py            allocate_kv_pool
+  nanopointllm/compression/quantized_tensor_package.py
+                                         write_quantized_linear_package (packages in
+                                         ref_linear_package_*/, written by the reference)
   transformers (installed 5.5.0)            LlamaRotaryEmbedding, apply_rotary_pos_emb
 """
 from __future__ import annotations
@@ -83,6 +86,29 @@ def main() -> None:
         lin_x=lin_x.numpy(), lin_w=lin_w.numpy(), lin_b=lin_b.numpy(), lin_s=lin_s.numpy(),
         lin_out=lin_out.numpy(), lin_acc=lin_acc.numpy(),
     )
+
+    # 1b. Linear packages written by the reference's own writer: the test's
+    # 2x4 / 3x4 case (tests/test_quantized_tensor_package.py:11-23) and a ragged
+    # seeded case with bias and output scale. They pin the loader and the
+    # byte-for-byte output of nanopointllm_b200.package's writer.
+    from nanopointllm.compression import quantized_tensor_package as QP
+    QP.write_quantized_linear_package(
+        HERE / "ref_linear_package_small", activation=pkg_a, weight=pkg_w,
+        activation_scale=np.array([0.125], dtype=np.float16),
+        weight_scale=np.array([0.25, 0.5, 1.0], dtype=np.float16),
+        smooth_scale=np.array([1.0, 2.0, 3.0, 4.0], dtype=np.float16),
+        output_scale=np.array([0.75], dtype=np.float16),
+        provenance={"module": "layers.0.self_attn.q_proj"})
+    rng = np.random.default_rng(21)
+    QP.write_quantized_linear_package(
+        HERE / "ref_linear_package_ragged",
+        activation=rng.integers(-127, 128, (3, 40), dtype=np.int8),
+        weight=rng.integers(-127, 128, (37, 40), dtype=np.int8),
+        activation_scale=0.0625,
+        weight_scale=(rng.random(37) * 0.01 + 1e-3).astype(np.float16),
+        smooth_scale=(rng.random(40) + 0.5).astype(np.float16),
+        output_scale=1.5, bias=(rng.standard_normal(37) * 0.1).astype(np.float16),
+        provenance={"module": "layers.3.mlp.down_proj", "seed": 21})
 
     # 2. Integer linear, small shapes, fp32 and fp16 inputs, per-token scale, +/- bias.
     small = {}

@@ -1,7 +1,7 @@
 """Tensor-parallel runner on 2 GPUs (NCCL, one process per GPU): prefill and
 greedy decode of the tiny Llama, eager and CUDA graph, bit-identical to the
-single-GPU W8A8LlamaRunner on the same weights (skipped with fewer than two
-GPUs)."""
+single-GPU W8A8LlamaRunner on the same weights, built from the float weights
+and from a checksummed int8 package (skipped with fewer than two GPUs)."""
 from __future__ import annotations
 
 import datetime
@@ -21,7 +21,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _rank_main(rank: int, world: int, port: int, errors) -> None:
+def _rank_main(rank: int, world: int, port: int, pkg_dir: str, errors) -> None:
     import torch.distributed as dist
     try:
         os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -47,6 +47,12 @@ def _rank_main(rank: int, world: int, port: int, errors) -> None:
             np.testing.assert_array_equal(t_tp, t_ref)
             np.testing.assert_array_equal(l_tp, l_ref)
             del run
+        run = TP.W8A8TPLlamaRunner.from_package(pkg_dir, device=dev, num_blocks=len(lengths) * per_seq,
+                                                block_size=bs)
+        t_tp, l_tp = _generate(run, prompts, bt, 5, dev, graph=True)
+        np.testing.assert_array_equal(t_tp, t_ref)
+        np.testing.assert_array_equal(l_tp, l_ref)
+        del run
         _lib.device_status()
         torch.cuda.synchronize()
         dist.barrier()
@@ -57,13 +63,28 @@ def _rank_main(rank: int, world: int, port: int, errors) -> None:
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_tp2_bit_identical_to_single_gpu():
+def test_tp2_bit_identical_to_single_gpu(tmp_path):
     import torch.multiprocessing as mp
+    from oracle import w8a8 as O
+    from nanopointllm_b200 import package as P, synthetic as S
+
+    class OracleWeights:  # the package's int8 weights, quantised on the host
+        def __init__(self, sd):
+            self.sd = sd
+
+        def linear(self, module):
+            q, s = O.per_output_weight_quant(self.sd[module + ".weight"].float().numpy())
+            return torch.from_numpy(q), torch.from_numpy(s.reshape(-1))
+
+        def dense(self, name):
+            return self.sd[name]
+
+    P.write_w8a8_llama_package(tmp_path, S.TINY, OracleWeights(S.llama_weights(S.TINY, seed=0)))
     world = 2
     ctx = mp.get_context("spawn")
     errors = ctx.SimpleQueue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, world, port, errors)) for r in range(world)]
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, str(tmp_path), errors)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
