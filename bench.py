@@ -30,7 +30,9 @@ summaries in profiles/ are taken with. Cases: qkv, o, gate_up,
 down, lm_head (decode linears, M = 8), attention (B = 8, context 1040),
 rmsnorm_quant, prefill (the five config-4 GEMMs at M = 4480), int8_peak
 (cuBLASLt int8 GEMM through torch._int_mm, 8192^3: the measured int8 tensor
-peak the prefill roofline is reported against), package_load (start-up of
+peak the prefill roofline is reported against), prefill_attention (the
+varlen prefill attention at config 4: 8 x 560 tokens, causal FLOP/s against
+the measured dense fp16/bf16 peak), package_load (start-up of
 a 7B-geometry runner with ``--layers`` layers from fp16 host weights against
 from the checksummed int8 package).
 
@@ -499,7 +501,7 @@ def cpu_baseline(seconds: float = 20.0) -> dict:
 
 # ------------------------------------------------------- single-op cases
 KERNEL_CASES = ("qkv", "o", "gate_up", "down", "lm_head", "attention", "rmsnorm_quant", "prefill", "int8_peak",
-                "package_load")
+                "prefill_attention", "package_load")
 
 
 def run_kernel_case(args, torch, device) -> dict:
@@ -595,6 +597,30 @@ def run_kernel_case(args, torch, device) -> dict:
         us = timed(lambda i: torch._int_mm(a, b), 1)
         line.update({"kernel": "cuBLASLt int8 GEMM (torch._int_mm)", "shape": [n, n, n],
                      "us_per_launch": round(us, 1), "tops": round(2 * n ** 3 / us / 1e6, 1)})
+    elif name == "prefill_attention":
+        # config 4: 8 prompts x 560 tokens prefilled in one step, 7B heads
+        n_seq, q_len, bs = 8, 560, BLOCK_SIZE
+        mb = -(-q_len // bs)
+        nb = n_seq * mb
+        k_cache = torch.randn(nb, bs, shape.kv_heads, shape.head_dim, device=device, generator=g).half()
+        v_cache = torch.randn(nb, bs, shape.kv_heads, shape.head_dim, device=device, generator=g).half()
+        bt = S.permuted_block_tables(n_seq, mb, nb, seed=1).to(device)
+        q = torch.randn(n_seq * q_len, shape.heads, shape.head_dim, device=device, generator=g).half()
+        lens = torch.full((n_seq,), q_len, dtype=torch.int32, device=device)
+        offs = torch.arange(0, n_seq * q_len, q_len, dtype=torch.int32, device=device)
+        out = torch.empty_like(q)
+        us = timed(lambda i: PA.paged_varlen_attention(q, k_cache, v_cache, bt, lens, lens, offs,
+                                                       shape.head_dim ** -0.5, 1, max_q_len=q_len, out=out), 1)
+        pairs = n_seq * shape.heads * q_len * (q_len + 1) // 2   # causal (query, key) pairs
+        flops = 4 * shape.head_dim * pairs                        # QK^T and P.V, 2 flops per MAC
+        pf = REPO / "MEASURED_PEAKS.json"
+        peak = float(json.loads(pf.read_text())["bf16_tflops"]) if pf.exists() else 1590.0
+        line.update({"kernel": "prefill_attn_kernel<128> (tcgen05 kind::f16)",
+                     "config": "config4 prefill: 8 x 560 tokens, H = 32, D = 128, block_size 256",
+                     "us_per_launch": round(us, 2), "tflops": round(flops / us / 1e6, 1),
+                     "causal_flops": flops, "peak_tflops": peak,
+                     "peak_kind": "measured" if pf.exists() else "fallback",
+                     "frac": round(flops / us / 1e6 / peak, 3)})
     elif name == "package_load":
         line.update(package_load_case(args, torch, device))
     L.device_status()

@@ -273,6 +273,28 @@ int npl_paged_decode_attention(const void* q, int B, int H, int Hkv, int D, cons
                                const int32_t* context_lens, float scale, void* out, int8_t* q_out_or_null,
                                float* q_scale_or_null, void* workspace, size_t workspace_bytes, void* stream);
 
+/*
+ * Causal varlen attention of multi-token rows (prefill and suffix prefill)
+ * over the paged pool: replaces paged_varlen_attention (paged_attention.py:
+ * 1142-1207; Triton kernel :1037-1139). q fp16 [total_q, H, D] (token stride
+ * ld_q elements, heads contiguous); sequence b owns rows
+ * [q_offsets[b], q_offsets[b] + q_lens[b]) and the first context_lens[b]
+ * slots of its block table; query j of it sits at absolute position
+ * context_lens[b] - q_lens[b] + j and sees keys 0..that position. Scores are
+ * fp32 dot products times `scale`; online softmax in fp32 with the
+ * probabilities rounded to fp16 for the P.V product (tcgen05 kind::f16, fp32
+ * accumulation). out fp16 [total_q, H, D] (token stride ld_out); rows of no
+ * sequence are not written. max_q_len >= every q_lens[b] sizes the launch.
+ * D is 64 or 128; block_size a multiple of 8. Bad table entries or offsets
+ * skip the access and set NPL_DEV code 5 (npl_device_status). No workspace,
+ * no allocation, no synchronisation (graph-capturable).
+ */
+int npl_paged_prefill_attention(const void* q, int ld_q, int total_q, int H, int Hkv, int D, const void* k_cache,
+                                const void* v_cache, int num_blocks, int block_size, const int32_t* block_tables,
+                                int bt_stride, int max_blocks, const int32_t* context_lens, const int32_t* q_lens,
+                                const int32_t* q_offsets, int B, int max_q_len, float scale, void* out, int ld_out,
+                                void* stream);
+
 #ifdef __cplusplus
 }
 #endif

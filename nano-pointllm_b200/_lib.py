@@ -73,6 +73,8 @@ SIGNATURES = {
     "npl_decode_attention_workspace_bytes": (_Z, [_I, _I, _I, _I, _I]),
     "npl_paged_decode_attention": (_I, [_P, _I, _I, _I, _I, _P, _P, _I, _I, _P, _I, _I, _P, _F, _P, _P, _P, _P, _Z,
                                         _P]),
+    "npl_paged_prefill_attention": (_I, [_P, _I, _I, _I, _I, _I, _P, _P, _I, _I, _P, _I, _I, _P, _P, _P, _I, _I, _F,
+                                         _P, _I, _P]),
 }
 
 

@@ -20,7 +20,7 @@
 namespace npl {
 namespace {
 
-constexpr int kDevBadIndex = 5;  // a slot, block or position outside its table
+constexpr int kDevBadIndex = NPL_DEV_BAD_INDEX;
 
 __device__ __forceinline__ void flag_bad_index(int* status) {
   if (status) atomicCAS(status, 0, kDevBadIndex);
@@ -168,15 +168,6 @@ struct AttnArgs {
   int32_t* work;      // [2]: next item beyond the first grid.x, CTAs done
   int* status;
 };
-
-__device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map, int c0, int c1, int c2,
-                                            uint64_t* bar, uint64_t policy) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
-      " [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(smem_u32(smem_dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar)), "l"(policy)
-      : "memory");
-}
 
 __device__ __forceinline__ void consumer_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 

@@ -94,6 +94,7 @@ enum DeviceError : int {
   NPL_DEV_TIMEOUT_MMA = 2,
   NPL_DEV_TIMEOUT_EPILOGUE = 3,
   NPL_DEV_TIMEOUT_TEARDOWN = 4,
+  NPL_DEV_BAD_INDEX = 5,  // a slot, block-table entry or position outside its table
 };
 
 constexpr float kFp16Tiny = 6.103515625e-05f;  // torch.finfo(torch.float16).tiny = 2^-14
@@ -292,6 +293,28 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
       : "memory");
 }
 
+// Orders this thread's generic-proxy shared-memory writes before later reads
+// of the same bytes through the async proxy (TMA, tcgen05.mma operands).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// 3-D tiled TMA load (c0 innermost, in elements), completion counted on `bar`.
+__device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map, int c0, int c1, int c2,
+                                            uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ uint64_t policy_evict_normal() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
 __device__ __forceinline__ uint64_t policy_evict_first() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
@@ -350,6 +373,17 @@ __device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t
       : "memory");
 }
 
+// D[tmem] (+)= A[smem] * B[smem], fp16 x fp16 -> fp32 (kind::f16).
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                        uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // 32 lanes x 8 consecutive 32-bit columns; thread i of the warp gets lane
@@ -359,6 +393,27 @@ __device__ __forceinline__ void tmem_ld_x8(uint32_t taddr, int32_t (&r)[8]) {
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
                  "=r"(r[7])
                : "r"(taddr));
+}
+
+// 32 lanes x 32 consecutive 32-bit columns; thread i of the warp gets lane
+// (base lane + i), columns [col, col + 32).
+__device__ __forceinline__ void tmem_ld_x32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
+// Instruction descriptor of kind::f16: fp16 A and B, fp32 accumulator
+// (c_format [4,6) = 1), a/b_format [7,10) / [10,13) = 0 (F16), A K-major,
+// B K-major (bit 16 = 0) or MN-major (bit 16 = 1), N >> 3 at [17,23),
+// M >> 4 at [24,29).
+__host__ __device__ constexpr uint32_t idesc_f16(int m, int n, bool b_mn_major) {
+  return (1u << 4) | ((b_mn_major ? 1u : 0u) << 16) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
 
 // Instruction descriptor of kind::i8: signed int8 A and B, both K-major, int32
@@ -377,6 +432,16 @@ __host__ __device__ constexpr uint32_t idesc_i8(int m, int n) {
 // [61,64). Advancing along K inside the 128 B row moves the start address.
 __device__ __forceinline__ uint64_t sdesc_k_sw128(uint32_t smem_addr) {
   return (uint64_t)((smem_addr >> 4) & 0x3FFFu) | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
+}
+
+// Shared-memory matrix descriptor for an MN-major operand stored with the
+// 128-byte swizzle: each K row holds 64 consecutive 16-bit MN elements in one
+// 128 B line (16 B chunks XOR (row % 8)), 8 K rows form a 1024 B atom. The
+// leading byte offset is the distance between 64-element MN chunks, the
+// stride byte offset the distance between 8-row K groups (both encoded >> 4).
+__device__ __forceinline__ uint64_t sdesc_mn_sw128(uint32_t smem_addr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+  return (uint64_t)((smem_addr >> 4) & 0x3FFFu) | ((uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16) |
+         ((uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
 }
 
 }  // namespace npl

@@ -2,6 +2,8 @@
 
 * ``store_kvcache``          - paged_attention.py:353-383 (same signature)
 * ``paged_decode_attention`` - paged_attention.py:872-1030 (same signature)
+* ``paged_varlen_attention`` - paged_attention.py:1142-1207 (same signature;
+                               causal prefill / suffix prefill from the pool)
 * ``rope_store_kvcache``     - paged_attention.py:1284-1294 (rotary_fn on q/k of
                                the packed QKV projection, then store_kvcache)
 
@@ -98,3 +100,45 @@ def paged_decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torc
         block_tables.stride(0), max_blocks, context_lens.data_ptr(), float(scale), out.data_ptr(), L.ptr(q8),
         L.ptr(qs), ws.data_ptr(), ws.numel(), L.stream_ptr(q.device)))
     return out
+
+
+def paged_varlen_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                           block_tables: torch.Tensor, context_lens: torch.Tensor, q_lens: torch.Tensor,
+                           q_offsets: torch.Tensor, scale: float, num_kv_groups: int,
+                           block_m: int | None = None, block_n: int | None = None, *,
+                           max_q_len: int | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Varlen paged attention for q_len > 1 prefill / suffix prefill
+    (paged_attention.py:1142-1207): q fp16 [total_q, H, D] -> [total_q, H, D].
+
+    ``block_m`` / ``block_n`` are accepted for signature compatibility with the
+    reference (its Triton tile sizes); the kernel uses 128 x 128 tiles.
+    ``max_q_len`` (>= every q_lens) avoids reading q_lens back to the host.
+    """
+    del block_m, block_n
+    _check_cache(k_cache, v_cache)
+    total_q, h, d = q.shape
+    nb, bs, hkv, dk = k_cache.shape
+    if dk != d or hkv * num_kv_groups != h:
+        raise ValueError("q / KV cache head geometry mismatch")
+    if total_q == 0:
+        return q.new_empty((0, h, d))
+    if q.dtype != torch.float16:
+        raise ValueError("q must be float16")
+    if q.stride(2) != 1 or q.stride(1) != d:
+        q = q.contiguous()
+    for t in (block_tables, context_lens, q_lens, q_offsets):
+        if t.dtype != torch.int32:
+            raise ValueError("block_tables, context_lens, q_lens and q_offsets must be int32")
+    block_tables = block_tables if block_tables.stride(1) == 1 else block_tables.contiguous()
+    context_lens, q_lens, q_offsets = context_lens.contiguous(), q_lens.contiguous(), q_offsets.contiguous()
+    if out is None:
+        out = torch.empty((total_q, h, d), dtype=torch.float16, device=q.device)
+    if max_q_len is None:
+        max_q_len = int(q_lens.max().item()) if q_lens.numel() else 0
+    L.check(L.lib.npl_paged_prefill_attention(
+        q.data_ptr(), q.stride(0), total_q, h, hkv, d, k_cache.data_ptr(), v_cache.data_ptr(), nb, bs,
+        block_tables.data_ptr(), block_tables.stride(0), block_tables.shape[1], context_lens.data_ptr(),
+        q_lens.data_ptr(), q_offsets.data_ptr(), q_lens.numel(), int(max_q_len), float(scale), out.data_ptr(),
+        out.stride(0), L.stream_ptr(q.device)))
+    return out
+

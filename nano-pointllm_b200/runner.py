@@ -29,8 +29,8 @@ the linears themselves -- the fp16-activation and RoPE modes of
 npl_w8a8_linear_ex -- measured slower on B200: it lengthens the linear's
 critical path by more than the small kernel costs.)
 
-Prefill attention over multi-token rows uses torch SDPA per sequence on the
-pool (the reference runs its own Triton varlen kernel there); the prefill
+Prefill attention over multi-token rows is npl_paged_prefill_attention (the
+tcgen05 replacement of the reference's Triton varlen kernel); the prefill
 linears are the same tcgen05 kernels at M = prefill tokens.
 """
 from __future__ import annotations
@@ -205,35 +205,33 @@ class W8A8LlamaRunner:
             out = PA.paged_decode_attention(q, layer.k_cache, layer.v_cache, ctx.block_tables, ctx.context_lens,
                                             self.scale, s.heads // s.kv_heads)
             return out.reshape(t, -1)
-        outs, off = [], 0
+        # mixed / prefill step (paged_attention.py:1379-1440): the multi-token
+        # rows of every sequence in one launch of the varlen prefill kernel,
+        # single-token rows through the decode kernel
         groups = s.heads // s.kv_heads
-        ctx_lens = ctx.context_lens.tolist()
-        for b, qlen in enumerate(ctx.seq_lens):
-            n = int(ctx_lens[b])
-            if qlen == 1:
-                o = PA.paged_decode_attention(q[off:off + 1], layer.k_cache, layer.v_cache,
-                                              ctx.block_tables[b:b + 1], ctx.context_lens[b:b + 1], self.scale, groups)
-                outs.append(o.reshape(1, -1))
-            else:
-                nblk = (n + self.block_size - 1) // self.block_size
-                bt = ctx.block_tables[b, :nblk].long()
-                k = layer.k_cache[bt].reshape(-1, s.kv_heads, s.head_dim)[:n]
-                v = layer.v_cache[bt].reshape(-1, s.kv_heads, s.head_dim)[:n]
-                # fp32 operands: the reference evaluates this attention with fp32
-                # accumulation and no fp16 rounding of the probabilities
-                qi = q[off:off + qlen].permute(1, 0, 2).unsqueeze(0).float()
-                ki = k.permute(1, 0, 2).unsqueeze(0).repeat_interleave(groups, 1).float()
-                vi = v.permute(1, 0, 2).unsqueeze(0).repeat_interleave(groups, 1).float()
-                prefix = n - qlen
-                if prefix == 0:
-                    o = F.scaled_dot_product_attention(qi, ki, vi, is_causal=True, scale=self.scale)
-                else:
-                    allowed = (torch.arange(n, device=q.device)[None, :]
-                               <= prefix + torch.arange(qlen, device=q.device)[:, None])
-                    o = F.scaled_dot_product_attention(qi, ki, vi, attn_mask=allowed, scale=self.scale)
-                outs.append(o[0].permute(1, 0, 2).reshape(qlen, -1).half())
-            off += qlen
-        return torch.cat(outs)
+        out = torch.empty((t, s.heads, s.head_dim), dtype=torch.float16, device=q.device)
+        offs = [0]
+        for n in ctx.seq_lens:
+            offs.append(offs[-1] + n)
+        pre = [i for i, n in enumerate(ctx.seq_lens) if n > 1]
+        dec = [i for i, n in enumerate(ctx.seq_lens) if n == 1]
+        dev = q.device
+        if pre:
+            rows = torch.tensor(pre, dtype=torch.long, device=dev)
+            PA.paged_varlen_attention(
+                q, layer.k_cache, layer.v_cache, ctx.block_tables.index_select(0, rows),
+                ctx.context_lens.index_select(0, rows),
+                torch.tensor([ctx.seq_lens[i] for i in pre], dtype=torch.int32, device=dev),
+                torch.tensor([offs[i] for i in pre], dtype=torch.int32, device=dev), self.scale, groups,
+                max_q_len=max(ctx.seq_lens[i] for i in pre), out=out)
+        if dec:
+            rows = torch.tensor(dec, dtype=torch.long, device=dev)
+            at = torch.tensor([offs[i] for i in dec], dtype=torch.long, device=dev)
+            o = PA.paged_decode_attention(q.index_select(0, at), layer.k_cache, layer.v_cache,
+                                          ctx.block_tables.index_select(0, rows), ctx.context_lens.index_select(0, rows),
+                                          self.scale, groups)
+            out.index_copy_(0, at, o)
+        return out.reshape(t, -1)
 
     # Optional per-op timing hook: timer(name, fn, *args, **kwargs) -> fn(...)
     # (used by bench.py to time each kernel with CUDA events on its stream).

@@ -6,7 +6,9 @@ Restates the eager reference path that the W8A8 golden is defined on:
 ``LightweightLlamaRunner.forward`` (lightweight_runner.py:625-736) with
 ``LightweightLlamaLayer.forward`` (:480-560, eager branch), ``PagedLlamaAttention``
 (paged_attention.py:1271-1488: q/k/v projections, rotary_fn, store_kvcache,
-per-sequence attention over the pool, o_proj), the non-packed MLP
+per-sequence attention over the pool -- float64 as on its CPU path, or its
+CUDA path's varlen prefill kernel, oracle.attention -- o_proj), the
+non-packed MLP
 (lightweight_runner.py:389-404), the final norm and the LM head, where every
 Linear is the integer golden of w8a8.py:118-139 on per-token dynamic int8
 activations and per-output-channel int8 weights.
@@ -15,6 +17,7 @@ from __future__ import annotations
 
 import numpy as np
 
+from . import attention as OA
 from . import w8a8 as O
 
 F16 = np.float16
@@ -22,7 +25,13 @@ F32 = np.float32
 
 
 class W8A8LlamaOracle:
-    def __init__(self, weights: dict, shape, k_cache_blocks: int, block_size: int):
+    def __init__(self, weights: dict, shape, k_cache_blocks: int, block_size: int, prefill: str = "exact"):
+        """prefill: "exact" evaluates multi-token rows in float64 (the
+        reference's CPU path, SDPA per sequence); "varlen" restates its CUDA
+        path, the Triton varlen kernel (oracle.attention)."""
+        if prefill not in ("exact", "varlen"):
+            raise ValueError("prefill must be 'exact' or 'varlen'")
+        self.prefill = prefill
         self.s = shape
         self.w = {k: np.asarray(v) for k, v in weights.items()}
         self.q = {}
@@ -51,7 +60,19 @@ class W8A8LlamaOracle:
         out = np.zeros((q.shape[0], s.heads, s.head_dim), np.float64)
         off = 0
         kc, vc = self.k_cache[layer], self.v_cache[layer]
+        starts = np.concatenate([[0], np.cumsum(seq_lens)[:-1]]).astype(np.int32)
+        if self.prefill == "varlen":  # paged_attention.py:1406-1433
+            pre = [b for b, n in enumerate(seq_lens) if n > 1]
+            if pre:
+                va = OA.paged_varlen_attention(
+                    q, kc, vc, np.asarray(block_tables)[pre], np.asarray(context_lens, np.int32)[pre],
+                    np.asarray(seq_lens, np.int32)[pre], starts[pre], scale, groups)
+                for b in pre:
+                    out[starts[b]:starts[b] + seq_lens[b]] = va[starts[b]:starts[b] + seq_lens[b]]
         for b, qlen in enumerate(seq_lens):
+            if self.prefill == "varlen" and qlen > 1:
+                off += qlen
+                continue
             n = int(context_lens[b])
             nblk = (n + self.block_size - 1) // self.block_size
             bt = block_tables[b, :nblk]

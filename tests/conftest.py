@@ -54,3 +54,21 @@ def cuda_device():
     if (major, minor) != (10, 0):
         pytest.fail(f"kernels are built for sm_100a, device is sm_{major}{minor}")
     return torch.device("cuda:0")
+
+
+def assert_match_until_tie(tokens, logits, ref_tokens, ref_logits, tie_tol, atol, min_steps=0):
+    """Per sequence: identical greedy tokens and logits within atol up to the
+    sequence's first differing token, which must be a near-tie of the
+    reference (its logits for the two tokens closer than tie_tol); later steps
+    of that sequence follow another history and are not compared."""
+    steps, batch = ref_tokens.shape
+    for b in range(batch):
+        diff = np.nonzero(tokens[:, b] != ref_tokens[:, b])[0]
+        stop = int(diff[0]) if diff.size else steps
+        np.testing.assert_allclose(logits[:stop + (stop < steps), b], ref_logits[:stop + (stop < steps), b],
+                                   atol=atol, rtol=0, err_msg=f"sequence {b}")
+        if stop < steps:
+            row = ref_logits[stop, b]
+            margin = abs(float(row[ref_tokens[stop, b]]) - float(row[tokens[stop, b]]))
+            assert margin < tie_tol, f"sequence {b} step {stop}: tokens differ with margin {margin}"
+        assert stop >= min_steps or stop == steps, f"sequence {b} diverged at step {stop}"
