@@ -10,29 +10,36 @@
 // and values are the first context_lens[b] slots of its block table in the
 // fp16 pool [num_blocks, block_size, Hkv, D]; query j sits at absolute
 // position context_len - q_len + j and attends to keys 0..that position.
-// Scores are fp32 dot products of the fp16 rows times `scale`, masked to the
-// lowest float; the softmax runs online over key tiles:
+// Scores are fp32 dot products of the fp16 rows times `scale` (> 0), masked
+// to the lowest float; the softmax runs online over key tiles:
 //   m' = max(m, rowmax(s));  p = exp(s - m');  alpha = exp(m - m')
 //   acc = acc * alpha + fp16(p) . V  (fp32 accumulation);  l = l * alpha + sum(p)
 // and out = fp16(acc / l). The probabilities are rounded to fp16 for the
 // P.V product and summed unrounded into l, as the reference does. Its key
-// tile is 64 (here 128), so the fp16 rounding of p, the exp and the order of
-// the fp32 sums differ: results agree to fp16 rounding, not bit for bit.
+// tile is 64 (here 128), exp(x) is evaluated here as exp2(x * log2(e)) with
+// the scale folded into one FMA, acc / l as acc * (1 / l), and the fp32 sums
+// run in another order: results agree to fp16 rounding, not bit for bit.
 //
-// One CTA per (128-query tile, sequence, head), 192 threads:
-//   warp 4      TMA: the Q tile once, then 128-key K and V tiles through the
-//               block table (2-stage ring; pieces of gcd(block_size, 128)
+// Persistent: one CTA per SM walks the (128-query tile, sequence, head)
+// items with a stride of the grid, longest first; the K/V rings, TMEM buffers
+// and barrier phases run on across items, so the next item's loads and
+// first Q.K^T overlap the current item's last tiles. 320 threads:
+//   warp 8      TMA: the Q tile once, then 128-key K and V tiles through the
+//               block table (2-stage rings; pieces of gcd(block_size, 128)
 //               keys, 128-byte swizzle); keys past the tile's last visible
 //               key are zero-filled out-of-bounds loads;
-//   warp 5      MMA issue (one thread): S_j = Q K_j^T into one of two TMEM
+//   warp 9      MMA issue (one thread): S_j = Q K_j^T into one of two TMEM
 //               buffers, then O_{j-1} = P_{j-1} V_{j-1} (V is the MN-major B
 //               operand: the cache layout as is) into one of two TMEM
 //               buffers, so the tensor core works on tile j while the
 //               softmax warps work on tile j-1;
-//   warps 0-3   one query row per thread (= TMEM lane): row max and
-//               exp of S_j, fp16 P_j into shared memory (K-major, 128-byte
-//               swizzle: the A operand of P.V), then acc = acc * alpha +
-//               O_{j-1} in registers, finally out = acc / l.
+//   warps 0-7   two warpgroups per query row (TMEM lane = row): group g
+//               takes keys [64g, 64g + 64) of each tile -- partial row max,
+//               combined with the other group's through shared memory, then
+//               exp and its half of fp16 P_j (K-major, 128-byte swizzle: the
+//               A operand of P.V) -- and the head-dimension half g of the
+//               output: acc = acc * alpha + O_{j-1} in registers, finally
+//               out = acc * (1 / l) (l summed per group, combined at the end).
 // TMEM: S at columns [0, 256), O at [256, 512).
 #include <algorithm>
 #include <cfloat>
@@ -46,9 +53,8 @@ namespace npl {
 namespace {
 
 constexpr int kPaTile = 128;
-constexpr int kPaThreads = 192;
+constexpr int kPaThreads = 320;  // warps 0-7 softmax, 8 TMA, 9 MMA
 constexpr uint32_t kPaTmemCols = 512;
-constexpr int kPaMaxQTiles = 65535;  // grid.x limit of the launch shape below
 
 template <int D>
 struct PaSmem {
@@ -58,11 +64,15 @@ struct PaSmem {
   alignas(1024) uint8_t q[kTileBytes];
   alignas(1024) uint8_t k[2][kTileBytes];
   alignas(1024) uint8_t v[2][kTileBytes];
-  alignas(1024) uint8_t p[2][kPBytes];
-  uint64_t q_full;
+  alignas(1024) uint8_t p[kPBytes];  // P of one key tile (the A operand of P.V)
+  uint64_t q_full, q_empty;
   uint64_t k_full[2], k_empty[2], v_full[2], v_empty[2];
-  uint64_t s_full[2], s_empty[2], p_full[2], p_empty[2], o_full[2], o_empty[2];
+  uint64_t s_full[2], s_empty[2], p_full, p_empty, o_full[2], o_empty[2];
   uint64_t mma_done;
+  uint64_t red_bar[2];           // the two softmax groups' partial maxima of a tile are in
+  uint64_t red_done;             // both partial normalisers are in
+  float red_max[2][2][kPaTile];  // [tile parity][key half][row]: partial row maxima
+  float red_l[2][kPaTile];       // [key half][row]: partial normalisers at the end
   uint32_t tmem_base;
   int abort;
 };
@@ -80,6 +90,14 @@ struct PaArgs {
   float scale;
   int* status;
 };
+
+// 2^x (ex2.approx.ftz: results below 2^-126 flush to 0; every p and alpha
+// here is such a value or one fp16 keeps, and a flushed term adds < 2^-126).
+__device__ __forceinline__ float pa_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 // mbar_wait that also gives up once another role of the CTA gave up.
 __device__ __forceinline__ bool pa_wait(uint64_t* bar, uint32_t parity, int* abort, int* status, int code) {
@@ -122,68 +140,67 @@ __device__ __forceinline__ void load_kv_tile(uint8_t* dst, const CUtensorMap* ma
   }
 }
 
-// acc = acc * alpha + O_i (TMEM buffer i & 1, this thread's lane).
+// acc = acc * alpha + O_i over this thread's half of the head dimension
+// (TMEM buffer i & 1, this thread's lane, columns [col0, col0 + D/2)).
 template <int D>
-__device__ __forceinline__ bool pa_correct(PaSmem<D>& s, float (&acc)[D], int i, float alpha, uint32_t o_tm,
+__device__ __forceinline__ bool pa_correct(PaSmem<D>& s, float (&acc)[D / 2], int i, float alpha, uint32_t o_tm,
                                            int* status) {
   const int ob = i & 1;
   if (!pa_wait(&s.o_full[ob], (i >> 1) & 1, &s.abort, status, NPL_DEV_TIMEOUT_EPILOGUE)) return false;
   tc_fence_after();
+  uint32_t v[D / 2];
 #pragma unroll
-  for (int c = 0; c < D / 32; ++c) {
-    uint32_t v[32];
-    tmem_ld_x32(o_tm + ob * 128 + c * 32, v);
-    tmem_wait_ld();
+  for (int c = 0; c < D / 64; ++c) tmem_ld_x32(o_tm + ob * 128 + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&v[c * 32]));
+  tmem_wait_ld();
 #pragma unroll
-    for (int e = 0; e < 32; ++e) acc[c * 32 + e] = fmaf(acc[c * 32 + e], alpha, __uint_as_float(v[e]));
-  }
+  for (int e = 0; e < D / 2; ++e) acc[e] = fmaf(acc[e], alpha, __uint_as_float(v[e]));
   tc_fence_before();
   mbar_arrive(&s.o_empty[ob]);
   return true;
 }
 
+// One work item: 128 query rows of one (sequence, head). Every role of the
+// CTA decodes the same items from the same read-only metadata, so all agree
+// on which items have work and how many key tiles each has.
+struct PaItem {
+  int b, h, q0, q_len, ctx, q_start, prefix, rows, kv_end, n_tiles;
+  bool skip;  // no query row of this item exists (or its offsets are invalid)
+};
+
+// Item i of the launch, longest first: items [0, B*H) are the last query
+// tiles of every (sequence, head), the next B*H the tiles before, and so on.
+__device__ __forceinline__ PaItem pa_item(const PaArgs& p, int i, int n_qtiles, int B) {
+  PaItem it;
+  const int bh = B * p.H;
+  const int level = i / bh, rem = i - level * bh;
+  it.b = rem / p.H;
+  it.h = rem - it.b * p.H;
+  it.q0 = (n_qtiles - 1 - level) * kPaTile;
+  it.q_len = p.q_lens[it.b];
+  it.skip = it.q0 >= it.q_len;
+  it.ctx = p.ctx_lens[it.b];
+  it.q_start = p.q_offsets[it.b];
+  it.prefix = it.ctx - it.q_len;
+  it.rows = min(kPaTile, it.q_len - it.q0);
+  it.kv_end = min(it.ctx, it.prefix + it.q0 + it.rows);  // keys some row of the item sees
+  it.n_tiles = it.kv_end > 0 ? (it.kv_end + kPaTile - 1) / kPaTile : 0;
+  if (!it.skip && (it.q_start < 0 || it.q_start > p.total_q - it.q_len)) it.skip = true;  // rows outside q / out
+  if (it.skip) it.n_tiles = 0;
+  return it;
+}
+
 template <int D>
 __global__ void __launch_bounds__(kPaThreads, 1)
     prefill_attn_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
-                        const __grid_constant__ CUtensorMap tmap_v, const PaArgs p) {
+                        const __grid_constant__ CUtensorMap tmap_v, const PaArgs p, int n_items, int n_qtiles,
+                        int B) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   PaSmem<D>& s = *reinterpret_cast<PaSmem<D>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int b = blockIdx.y, h = blockIdx.z;
-  const int q0 = (gridDim.x - 1 - blockIdx.x) * kPaTile;  // longest tiles first
-
-  pdl_wait();  // q, the pool and the metadata come from earlier work on the stream
-  const int q_len = p.q_lens[b];
-  if (q0 >= q_len) {
-    pdl_trigger();
-    return;
-  }
-  const int ctx = p.ctx_lens[b];
-  const int q_start = p.q_offsets[b];
-  if (q_start < 0 || q_start > p.total_q - q_len) {  // rows outside q / out: skip the sequence
-    if (threadIdx.x == 0) atomicCAS(p.status, 0, NPL_DEV_BAD_INDEX);
-    pdl_trigger();
-    return;
-  }
-  const int prefix = ctx - q_len;
-  const int rows = min(kPaTile, q_len - q0);
-  const int kv_end = min(ctx, prefix + q0 + rows);  // keys some row of the tile sees
-  const int n_tiles = kv_end > 0 ? (kv_end + kPaTile - 1) / kPaTile : 0;
-  if (prefix < 0 || ctx > p.max_blocks * p.block_size) {
-    if (threadIdx.x == 0) atomicCAS(p.status, 0, NPL_DEV_BAD_INDEX);
-  }
-  if (n_tiles == 0) {  // no visible key: the reference's masked loads make the output 0
-    if (threadIdx.x < rows) {
-      uint4* dst = reinterpret_cast<uint4*>(p.out + (size_t)(q_start + q0 + threadIdx.x) * p.ld_out + (size_t)h * D);
-#pragma unroll
-      for (int c = 0; c < D / 8; ++c) dst[c] = make_uint4(0, 0, 0, 0);
-    }
-    pdl_trigger();
-    return;
-  }
 
   if (threadIdx.x == 0) {
     mbar_init(&s.q_full, 1);
+    mbar_init(&s.q_empty, 1);
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s.k_full[i], 1);
@@ -191,17 +208,20 @@ __global__ void __launch_bounds__(kPaThreads, 1)
       mbar_init(&s.v_full[i], 1);
       mbar_init(&s.v_empty[i], 1);
       mbar_init(&s.s_full[i], 1);
-      mbar_init(&s.s_empty[i], 128);
-      mbar_init(&s.p_full[i], 128);
-      mbar_init(&s.p_empty[i], 1);
+      mbar_init(&s.s_empty[i], 256);
       mbar_init(&s.o_full[i], 1);
-      mbar_init(&s.o_empty[i], 128);
+      mbar_init(&s.o_empty[i], 256);
     }
+    mbar_init(&s.p_full, 256);
+    mbar_init(&s.p_empty, 1);
     mbar_init(&s.mma_done, 1);
+    mbar_init(&s.red_bar[0], 256);
+    mbar_init(&s.red_bar[1], 256);
+    mbar_init(&s.red_done, 256);
     s.abort = 0;
     fence_mbar_init();
   }
-  if (warp == 5) {
+  if (warp == 9) {
     tmem_alloc(&s.tmem_base, kPaTmemCols);
     tmem_relinquish();
   }
@@ -209,9 +229,10 @@ __global__ void __launch_bounds__(kPaThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = s.tmem_base;
+  pdl_wait();  // q, the pool and the metadata come from earlier work on the stream
   pdl_trigger();
 
-  if (warp == 4) {
+  if (warp == 8) {
     // ------------------------------------------------------------ TMA
     if (lane == 0) {
       prefetch_tensormap(&tmap_q);
@@ -219,51 +240,66 @@ __global__ void __launch_bounds__(kPaThreads, 1)
       prefetch_tensormap(&tmap_v);
       const uint64_t pol_q = policy_evict_first();
       const uint64_t pol_kv = policy_evict_normal();  // re-read by the other query tiles of the sequence
-      const int kvh = h / (p.H / p.Hkv);
       const int oob = p.num_blocks * p.block_size;
-      const int32_t* table = p.bt + (size_t)b * p.bt_stride;
-      mbar_arrive_expect_tx(&s.q_full, PaSmem<D>::kTileBytes);
+      int kt = 0, nk = 0, nv = 0, nq = 0;  // tiles of this CTA so far; K, V tiles and Q tiles issued
+      bool ok = true;
+      for (int i = blockIdx.x; ok && i < n_items; i += gridDim.x) {
+        const PaItem it = pa_item(p, i, n_qtiles, B);
+        if (it.n_tiles == 0) continue;
+        if (it.prefix < 0 || it.ctx > p.max_blocks * p.block_size) atomicCAS(p.status, 0, NPL_DEV_BAD_INDEX);
+        const int kvh = it.h / (p.H / p.Hkv);
+        const int32_t* table = p.bt + (size_t)it.b * p.bt_stride;
+        if (nq > 0 && !pa_wait(&s.q_empty, (nq - 1) & 1, &s.abort, p.status, NPL_DEV_TIMEOUT_TMA)) break;
+        mbar_arrive_expect_tx(&s.q_full, PaSmem<D>::kTileBytes);
 #pragma unroll
-      for (int hf = 0; hf < D / 64; ++hf)
-        tma_load_3d(s.q + hf * PaSmem<D>::kHalf, &tmap_q, hf * 64, h, q_start + q0, &s.q_full, pol_q);
-      int nk = 0, nv = 0;  // K and V tiles issued
-      for (int j = 0; j < n_tiles; ++j) {
-        const int st = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        if (!pa_wait(&s.k_empty[st], ph ^ 1, &s.abort, p.status, NPL_DEV_TIMEOUT_TMA)) break;
-        mbar_arrive_expect_tx(&s.k_full[st], PaSmem<D>::kTileBytes);
-        load_kv_tile<D>(s.k[st], &tmap_k, p, table, j, kv_end, kvh, oob, &s.k_full[st], pol_kv);
-        nk = j + 1;
-        if (!pa_wait(&s.v_empty[st], ph ^ 1, &s.abort, p.status, NPL_DEV_TIMEOUT_TMA)) break;
-        mbar_arrive_expect_tx(&s.v_full[st], PaSmem<D>::kTileBytes);
-        load_kv_tile<D>(s.v[st], &tmap_v, p, table, j, kv_end, kvh, oob, &s.v_full[st], pol_kv);
-        nv = j + 1;
+        for (int hf = 0; hf < D / 64; ++hf)
+          tma_load_3d(s.q + hf * PaSmem<D>::kHalf, &tmap_q, hf * 64, it.h, it.q_start + it.q0, &s.q_full, pol_q);
+        ++nq;
+        for (int j = 0; j < it.n_tiles; ++j, ++kt) {
+          const int st = kt & 1;
+          const uint32_t ph = (kt >> 1) & 1;
+          if (!pa_wait(&s.k_empty[st], ph ^ 1, &s.abort, p.status, NPL_DEV_TIMEOUT_TMA)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&s.k_full[st], PaSmem<D>::kTileBytes);
+          load_kv_tile<D>(s.k[st], &tmap_k, p, table, j, it.kv_end, kvh, oob, &s.k_full[st], pol_kv);
+          nk = kt + 1;
+          if (!pa_wait(&s.v_empty[st], ph ^ 1, &s.abort, p.status, NPL_DEV_TIMEOUT_TMA)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&s.v_full[st], PaSmem<D>::kTileBytes);
+          load_kv_tile<D>(s.v[st], &tmap_v, p, table, j, it.kv_end, kvh, oob, &s.v_full[st], pol_kv);
+          nv = kt + 1;
+        }
       }
       // Drain: every load issued here has landed before the CTA may exit
       // (already true unless a role gave up). The last load of each stage is
       // the newest phase of its barrier.
-      mbar_wait(&s.q_full, 0, p.status, NPL_DEV_TIMEOUT_TEARDOWN);
+      if (nq > 0) mbar_wait(&s.q_full, (nq - 1) & 1, p.status, NPL_DEV_TIMEOUT_TEARDOWN);
       for (int j = max(0, nk - 2); j < nk; ++j)
         mbar_wait(&s.k_full[j & 1], (j >> 1) & 1, p.status, NPL_DEV_TIMEOUT_TEARDOWN);
       for (int j = max(0, nv - 2); j < nv; ++j)
         mbar_wait(&s.v_full[j & 1], (j >> 1) & 1, p.status, NPL_DEV_TIMEOUT_TEARDOWN);
     }
     __syncwarp();
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     // ------------------------------------------------------------ MMA
     if (lane == 0) {
       constexpr uint32_t kIdQK = idesc_f16(kPaTile, kPaTile, false);
       constexpr uint32_t kIdPV = idesc_f16(kPaTile, D, true);
       const uint32_t q_addr = smem_u32(s.q);
-      auto issue_pv = [&](int i) -> bool {
-        const int pb = i & 1;
-        const uint32_t ph = (i >> 1) & 1;
-        if (!pa_wait(&s.p_full[pb], ph, &s.abort, p.status, NPL_DEV_TIMEOUT_MMA) ||
+      // O_t = P_t V_t for the global tile index t of this CTA
+      auto issue_pv = [&](int t) -> bool {
+        const int pb = t & 1;
+        const uint32_t ph = (t >> 1) & 1;
+        if (!pa_wait(&s.p_full, t & 1, &s.abort, p.status, NPL_DEV_TIMEOUT_MMA) ||
             !pa_wait(&s.v_full[pb], ph, &s.abort, p.status, NPL_DEV_TIMEOUT_MMA) ||
             !pa_wait(&s.o_empty[pb], ph ^ 1, &s.abort, p.status, NPL_DEV_TIMEOUT_MMA))
           return false;
         tc_fence_after();
-        const uint32_t pa = smem_u32(s.p[pb]), va = smem_u32(s.v[pb]);
+        const uint32_t pa = smem_u32(s.p), va = smem_u32(s.v[pb]);
 #pragma unroll
         for (int kk = 0; kk < kPaTile / 16; ++kk) {
           const uint64_t ad = sdesc_k_sw128(pa + (kk >> 2) * PaSmem<D>::kHalf + (kk & 3) * 32);
@@ -271,150 +307,197 @@ __global__ void __launch_bounds__(kPaThreads, 1)
           mma_f16(tmem + 256 + pb * 128, ad, bd, kIdPV, kk > 0 ? 1u : 0u);
         }
         tc_commit(&s.o_full[pb]);
-        tc_commit(&s.p_empty[pb]);
+        tc_commit(&s.p_empty);
         tc_commit(&s.v_empty[pb]);
         return true;
       };
-      bool ok = pa_wait(&s.q_full, 0, &s.abort, p.status, NPL_DEV_TIMEOUT_MMA);
-      for (int j = 0; ok && j < n_tiles; ++j) {
-        const int st = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        if (!pa_wait(&s.k_full[st], ph, &s.abort, p.status, NPL_DEV_TIMEOUT_MMA) ||
-            !pa_wait(&s.s_empty[st], ph ^ 1, &s.abort, p.status, NPL_DEV_TIMEOUT_MMA)) {
+      bool ok = true;
+      int kt = 0, nq = 0, pending = -1;  // pending: tile whose P.V is issued after the next Q.K^T
+      for (int i = blockIdx.x; ok && i < n_items; i += gridDim.x) {
+        const PaItem it = pa_item(p, i, n_qtiles, B);
+        if (it.n_tiles == 0) continue;
+        if (!pa_wait(&s.q_full, nq & 1, &s.abort, p.status, NPL_DEV_TIMEOUT_MMA)) {
           ok = false;
           break;
         }
-        tc_fence_after();
-        const uint32_t ka = smem_u32(s.k[st]);
+        ++nq;
+        for (int j = 0; j < it.n_tiles; ++j, ++kt) {
+          const int st = kt & 1;
+          const uint32_t ph = (kt >> 1) & 1;
+          if (!pa_wait(&s.k_full[st], ph, &s.abort, p.status, NPL_DEV_TIMEOUT_MMA) ||
+              !pa_wait(&s.s_empty[st], ph ^ 1, &s.abort, p.status, NPL_DEV_TIMEOUT_MMA)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t ka = smem_u32(s.k[st]);
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * PaSmem<D>::kHalf + (kk & 3) * 32;
-          mma_f16(tmem + st * 128, sdesc_k_sw128(q_addr + off), sdesc_k_sw128(ka + off), kIdQK,
-                  kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * PaSmem<D>::kHalf + (kk & 3) * 32;
+            mma_f16(tmem + st * 128, sdesc_k_sw128(q_addr + off), sdesc_k_sw128(ka + off), kIdQK,
+                    kk > 0 ? 1u : 0u);
+          }
+          tc_commit(&s.s_full[st]);
+          tc_commit(&s.k_empty[st]);
+          if (j == it.n_tiles - 1) tc_commit(&s.q_empty);  // the item's Q is no longer read
+          if (pending >= 0 && !issue_pv(pending)) {
+            ok = false;
+            break;
+          }
+          pending = kt;
         }
-        tc_commit(&s.s_full[st]);
-        tc_commit(&s.k_empty[st]);
-        if (j > 0) ok = issue_pv(j - 1);
       }
-      if (ok) issue_pv(n_tiles - 1);
+      if (ok && pending >= 0) issue_pv(pending);
       tc_commit(&s.mma_done);  // arrives once every MMA issued above has completed
       mbar_wait(&s.mma_done, 0, p.status, NPL_DEV_TIMEOUT_TEARDOWN);
     }
     __syncwarp();
   } else {
     // -------------------------------------------- softmax and correction
-    const int r = threadIdx.x;  // query row of the tile = TMEM lane
-    const uint32_t lane_tm = tmem + ((uint32_t)(warp * 32) << 16);
-    const int q_row = q0 + r;
-    const int lim = q_row < q_len ? min(ctx, prefix + q_row + 1) : 0;  // keys [0, lim) visible
+    // Two warpgroups share every query row: group g owns keys [64g, 64g + 64)
+    // of each key tile (its half of P) and the head-dimension half
+    // [g D/2, (g+1) D/2) of the output; the row max is combined per tile
+    // through shared memory, the normaliser once per item.
+    const int g = warp >> 2;
+    const int r = threadIdx.x & 127;  // query row of the item = TMEM lane
+    const uint32_t lane_tm = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+    const uint32_t o_tm = lane_tm + 256 + g * (D / 2);
     const int swz = r & 7;
     const uint32_t prow = (uint32_t)(r >> 3) * 1024 + (uint32_t)swz * 128;
-    float acc[D];
-#pragma unroll
-    for (int c = 0; c < D; ++c) acc[c] = 0.f;
-    float m = -FLT_MAX, l = 0.f, alpha_prev = 0.f;
+    const float c2 = p.scale * 1.4426950408889634f;  // scale * log2(e)
     bool ok = true;
-    for (int j = 0; j < n_tiles; ++j) {
-      const int sb = j & 1;
-      const uint32_t ph = (j >> 1) & 1;
-      if (!pa_wait(&s.s_full[sb], ph, &s.abort, p.status, NPL_DEV_TIMEOUT_EPILOGUE)) {
-        ok = false;
-        break;
+    int kt = 0, nitems = 0;
+    for (int i = blockIdx.x; ok && i < n_items; i += gridDim.x) {
+      const PaItem it = pa_item(p, i, n_qtiles, B);
+      if (it.skip) {
+        if (it.q0 < it.q_len && threadIdx.x == 0) atomicCAS(p.status, 0, NPL_DEV_BAD_INDEX);
+        continue;
       }
-      tc_fence_after();
-      const uint32_t s_tm = lane_tm + sb * 128;
-      const int kb = j * kPaTile;
-      float mx = -FLT_MAX;
-#pragma unroll 1
-      for (int c = 0; c < kPaTile / 32; ++c) {
-        uint32_t v[32];
-        tmem_ld_x32(s_tm + c * 32, v);
-        tmem_wait_ld();
+      const int q_row = it.q0 + r;
+      __half* const dst_row = p.out + (size_t)(it.q_start + q_row) * p.ld_out + (size_t)it.h * D + g * (D / 2);
+      if (it.n_tiles == 0) {  // no visible key: the reference's masked loads make the output 0
+        if (q_row < it.q_len) {
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const float x = kb + c * 32 + e < lim ? __fmul_rn(__uint_as_float(v[e]), p.scale) : -FLT_MAX;
-          mx = fmaxf(mx, x);
+          for (int c = 0; c < D / 16; ++c) reinterpret_cast<uint4*>(dst_row)[c] = make_uint4(0, 0, 0, 0);
         }
+        continue;
       }
-      const float m_new = fmaxf(m, mx);
-      if (j >= 2 && !pa_wait(&s.p_empty[sb], ((j >> 1) - 1) & 1, &s.abort, p.status, NPL_DEV_TIMEOUT_EPILOGUE)) {
-        ok = false;
-        break;
-      }
-      uint8_t* const pbuf = s.p[sb];
-      float lsum = 0.f;
-#pragma unroll 1
-      for (int c = 0; c < kPaTile / 32; ++c) {
-        uint32_t v[32];
-        tmem_ld_x32(s_tm + c * 32, v);
-        tmem_wait_ld();
-        uint32_t packed[16];
+      const int lim = q_row < it.q_len ? min(it.ctx, it.prefix + q_row + 1) : 0;  // keys [0, lim) visible
+      float acc[D / 2];
 #pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          const int pos = kb + c * 32 + e;
-          const float x0 = pos < lim ? __fmul_rn(__uint_as_float(v[e]), p.scale) : -FLT_MAX;
-          const float x1 = pos + 1 < lim ? __fmul_rn(__uint_as_float(v[e + 1]), p.scale) : -FLT_MAX;
-          const float p0 = __expf(x0 - m_new), p1 = __expf(x1 - m_new);
-          lsum += p0;
-          lsum += p1;
-          const __half2 hp = __floats2half2_rn(p0, p1);
-          packed[e >> 1] = *reinterpret_cast<const uint32_t*>(&hp);
-        }
-#pragma unroll
-        for (int qd = 0; qd < 4; ++qd) {
-          const int c8 = c * 4 + qd;  // 8-key chunk of the row
-          *reinterpret_cast<uint4*>(pbuf + (c8 >> 3) * PaSmem<D>::kHalf + prow + (((c8 & 7) ^ swz) << 4)) =
-              make_uint4(packed[qd * 4], packed[qd * 4 + 1], packed[qd * 4 + 2], packed[qd * 4 + 3]);
-        }
-      }
-      tc_fence_before();
-      mbar_arrive(&s.s_empty[sb]);
-      const float alpha = __expf(m - m_new);
-      l = fmaf(l, alpha, lsum);
-      m = m_new;
-      if (j == n_tiles - 1 && kv_end < kb + kPaTile) {
-        // keys past the context in the last tile: zero their V rows (pool
-        // slots that may hold anything) so that 0-probability keys add 0
-        if (!pa_wait(&s.v_full[sb], ph, &s.abort, p.status, NPL_DEV_TIMEOUT_EPILOGUE)) {
+      for (int c = 0; c < D / 2; ++c) acc[c] = 0.f;
+      float m = -FLT_MAX, l = 0.f, alpha_prev = 0.f;  // m: running max of the raw scores
+      for (int j = 0; j < it.n_tiles; ++j) {
+        const int t = kt + j;  // this CTA's tile index: ring, buffer and phase selector
+        const int sb = t & 1;
+        const uint32_t ph = (t >> 1) & 1;
+        if (!pa_wait(&s.s_full[sb], ph, &s.abort, p.status, NPL_DEV_TIMEOUT_EPILOGUE)) {
           ok = false;
           break;
         }
-        if (r >= kv_end - kb) {
+        tc_fence_after();
+        const int kb = j * kPaTile + g * 64;  // first key of this thread's half tile
+        uint32_t v[64];
+        tmem_ld_x32(lane_tm + sb * 128 + g * 64, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+        tmem_ld_x32(lane_tm + sb * 128 + g * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+        tmem_wait_ld();
+        // Scores stay raw: max(s * scale) = max(s) * scale for scale > 0, and
+        // exp(s * scale - m') = exp2(fma(s, c2, -m_raw' * c2)), c2 = scale * log2(e).
+        if (kb + 64 > lim) {
 #pragma unroll
-          for (int hf = 0; hf < D / 64; ++hf) {
-            uint4* row = reinterpret_cast<uint4*>(s.v[sb] + hf * PaSmem<D>::kHalf + r * 128);
+          for (int e = 0; e < 64; ++e)
+            if (kb + e >= lim) v[e] = __float_as_uint(-FLT_MAX);
+        }
+        float mxp[8];  // independent partial maxima (short dependency chains)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) mxp[e] = __uint_as_float(v[e]);
+#pragma unroll
+        for (int e = 8; e < 64; ++e) mxp[e & 7] = fmaxf(mxp[e & 7], __uint_as_float(v[e]));
+        s.red_max[sb][g][r] = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
+                                    fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
+        mbar_arrive(&s.red_bar[sb]);  // release: the partial max above is visible to the waiters
+        if (!pa_wait(&s.red_bar[sb], ph, &s.abort, p.status, NPL_DEV_TIMEOUT_EPILOGUE)) {
+          ok = false;
+          break;
+        }
+        const float m_new = fmaxf(m, fmaxf(s.red_max[sb][0][r], s.red_max[sb][1][r]));
+        const float neg_mc = -m_new * c2;
+        if (t >= 1 && !pa_wait(&s.p_empty, (t - 1) & 1, &s.abort, p.status, NPL_DEV_TIMEOUT_EPILOGUE)) {
+          ok = false;
+          break;
+        }
+        float lsp[8];  // independent partial sums
+#pragma unroll
+        for (int e = 0; e < 8; ++e) lsp[e] = 0.f;
+        uint32_t packed[32];
+#pragma unroll
+        for (int e = 0; e < 64; e += 2) {
+          const float p0 = pa_exp2(fmaf(__uint_as_float(v[e]), c2, neg_mc));
+          const float p1 = pa_exp2(fmaf(__uint_as_float(v[e + 1]), c2, neg_mc));
+          lsp[(e >> 1) & 7] += p0;
+          lsp[((e >> 1) + 4) & 7] += p1;
+          const __half2 hp = __floats2half2_rn(p0, p1);
+          packed[e >> 1] = *reinterpret_cast<const uint32_t*>(&hp);
+        }
+        uint8_t* const pbuf = s.p + g * PaSmem<D>::kHalf;
+#pragma unroll
+        for (int c8 = 0; c8 < 8; ++c8)  // 8-key chunks of the row's half
+          *reinterpret_cast<uint4*>(pbuf + prow + ((c8 ^ swz) << 4)) =
+              make_uint4(packed[c8 * 4], packed[c8 * 4 + 1], packed[c8 * 4 + 2], packed[c8 * 4 + 3]);
+        tc_fence_before();
+        mbar_arrive(&s.s_empty[sb]);
+        const float lsum = ((lsp[0] + lsp[1]) + (lsp[2] + lsp[3])) + ((lsp[4] + lsp[5]) + (lsp[6] + lsp[7]));
+        const float alpha = pa_exp2(fmaf(m, c2, neg_mc));
+        l = fmaf(l, alpha, lsum);
+        m = m_new;
+        const int tile0 = j * kPaTile;
+        if (j == it.n_tiles - 1 && it.kv_end < tile0 + kPaTile && g < D / 64) {
+          // keys past the context in the last tile: zero their V rows (pool
+          // slots that may hold anything) so that 0-probability keys add 0
+          if (!pa_wait(&s.v_full[sb], ph, &s.abort, p.status, NPL_DEV_TIMEOUT_EPILOGUE)) {
+            ok = false;
+            break;
+          }
+          if (r >= it.kv_end - tile0) {
+            uint4* row = reinterpret_cast<uint4*>(s.v[sb] + g * PaSmem<D>::kHalf + r * 128);
 #pragma unroll
             for (int c = 0; c < 8; ++c) row[c] = make_uint4(0, 0, 0, 0);
           }
         }
-      }
-      fence_proxy_async_smem();
-      mbar_arrive(&s.p_full[sb]);
-      if (j > 0 && !pa_correct<D>(s, acc, j - 1, alpha_prev, lane_tm + 256, p.status)) {
-        ok = false;
-        break;
-      }
-      alpha_prev = alpha;
-    }
-    if (ok) ok = pa_correct<D>(s, acc, n_tiles - 1, alpha_prev, lane_tm + 256, p.status);
-    if (ok && q_row < q_len) {
-      uint4* dst = reinterpret_cast<uint4*>(p.out + (size_t)(q_start + q_row) * p.ld_out + (size_t)h * D);
-#pragma unroll
-      for (int c = 0; c < D / 8; ++c) {
-        uint32_t w[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const __half2 hv = __floats2half2_rn(__fdiv_rn(acc[c * 8 + 2 * e], l), __fdiv_rn(acc[c * 8 + 2 * e + 1], l));
-          w[e] = *reinterpret_cast<const uint32_t*>(&hv);
+        fence_proxy_async_smem();
+        mbar_arrive(&s.p_full);
+        if (j > 0 && !pa_correct<D>(s, acc, t - 1, alpha_prev, o_tm, p.status)) {
+          ok = false;
+          break;
         }
-        dst[c] = make_uint4(w[0], w[1], w[2], w[3]);
+        alpha_prev = alpha;
       }
+      if (ok) ok = pa_correct<D>(s, acc, kt + it.n_tiles - 1, alpha_prev, o_tm, p.status);
+      s.red_l[g][r] = l;
+      mbar_arrive(&s.red_done);  // every softmax thread arrives once per item, whatever happened above
+      if (ok) ok = pa_wait(&s.red_done, nitems & 1, &s.abort, p.status, NPL_DEV_TIMEOUT_EPILOGUE);
+      const float inv_l = __frcp_rn(s.red_l[0][r] + s.red_l[1][r]);  // out = acc * (1 / l)
+      if (ok && q_row < it.q_len) {
+#pragma unroll
+        for (int c = 0; c < D / 16; ++c) {
+          uint32_t w[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const __half2 hv = __floats2half2_rn(__fmul_rn(acc[c * 8 + 2 * e], inv_l),
+                                                 __fmul_rn(acc[c * 8 + 2 * e + 1], inv_l));
+            w[e] = *reinterpret_cast<const uint32_t*>(&hv);
+          }
+          reinterpret_cast<uint4*>(dst_row)[c] = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      }
+      kt += it.n_tiles;
+      ++nitems;
     }
   }
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     tc_fence_after();
     tmem_dealloc(tmem, kPaTmemCols);
   }
@@ -464,8 +547,11 @@ int launch_prefill(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorM
   const int smem = (int)sizeof(PaSmem<D>) + 1024;
   if (cudaFuncSetAttribute(prefill_attn_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return launch_status("npl_paged_prefill_attention: smem attribute");
-  return launch_pdl("npl_paged_prefill_attention", prefill_attn_kernel<D>, dim3(n_qtiles, B, p.H),
-                    dim3(kPaThreads), (size_t)smem, st, tq, tk, tv, p);
+  const long long items = (long long)n_qtiles * B * p.H;
+  const int sms = num_sms();
+  const int grid = (int)std::min<long long>(items, sms > 0 ? sms : 148);  // persistent: one CTA per SM
+  return launch_pdl("npl_paged_prefill_attention", prefill_attn_kernel<D>, dim3(grid), dim3(kPaThreads),
+                    (size_t)smem, st, tq, tk, tv, p, (int)items, n_qtiles, B);
 }
 
 }  // namespace
@@ -488,6 +574,8 @@ extern "C" int npl_paged_prefill_attention(const void* q, int ld_q, int total_q,
     return fail(NPL_ERR_ARG, "npl_paged_prefill_attention: bad shape");
   if (D != 128 && D != 64)
     return fail(NPL_ERR_UNSUPPORTED, "npl_paged_prefill_attention: head_dim %d (64 or 128)", D);
+  if (!(scale > 0.f) || !(scale < 3.0e38f))
+    return fail(NPL_ERR_ARG, "npl_paged_prefill_attention: scale must be positive and finite");
   if (block_size % 8)
     return fail(NPL_ERR_UNSUPPORTED, "npl_paged_prefill_attention: block_size %d (a multiple of 8)", block_size);
   if ((long long)num_blocks * block_size >= (1ll << 31) || (long long)max_blocks * block_size >= (1ll << 31) ||
@@ -497,8 +585,8 @@ extern "C" int npl_paged_prefill_attention(const void* q, int ld_q, int total_q,
     if (!aligned16(p)) return fail(NPL_ERR_ARG, "npl_paged_prefill_attention: pointers must be 16-byte aligned");
   if (B == 0 || total_q == 0 || max_q_len == 0) return NPL_OK;
   const int n_qtiles = (max_q_len + kPaTile - 1) / kPaTile;
-  if (n_qtiles > kPaMaxQTiles || B > 65535 || H > 65535)
-    return fail(NPL_ERR_UNSUPPORTED, "npl_paged_prefill_attention: launch shape too large");
+  if ((long long)n_qtiles * B * H >= (1ll << 31))
+    return fail(NPL_ERR_UNSUPPORTED, "npl_paged_prefill_attention: too many (query tile, sequence, head) items");
   const int piece = gcd_int(block_size, kPaTile);
   CUtensorMap tq, tk, tv;
   if (int rc = make_rows_map(&tq, q, total_q, H, D, ld_q, kPaTile, "q")) return rc;
