@@ -598,8 +598,8 @@ def run_kernel_case(args, torch, device) -> dict:
         line.update({"kernel": "cuBLASLt int8 GEMM (torch._int_mm)", "shape": [n, n, n],
                      "us_per_launch": round(us, 1), "tops": round(2 * n ** 3 / us / 1e6, 1)})
     elif name == "prefill_attention":
-        # config 4: 8 prompts x 560 tokens prefilled in one step, 7B heads
-        n_seq, q_len, bs = 8, 560, BLOCK_SIZE
+        # config 4 by default: 8 prompts x 560 tokens prefilled in one step, 7B heads
+        n_seq, q_len, bs = args.prefill_seqs, args.prefill_len, BLOCK_SIZE
         mb = -(-q_len // bs)
         nb = n_seq * mb
         k_cache = torch.randn(nb, bs, shape.kv_heads, shape.head_dim, device=device, generator=g).half()
@@ -616,7 +616,8 @@ def run_kernel_case(args, torch, device) -> dict:
         pf = REPO / "MEASURED_PEAKS.json"
         peak = float(json.loads(pf.read_text())["bf16_tflops"]) if pf.exists() else 1590.0
         line.update({"kernel": "prefill_attn_kernel<128> (tcgen05 kind::f16)",
-                     "config": "config4 prefill: 8 x 560 tokens, H = 32, D = 128, block_size 256",
+                     "config": f"prefill: {n_seq} x {q_len} tokens, H = 32, D = 128, block_size 256"
+                               + (" (config4)" if (n_seq, q_len) == (8, 560) else ""),
                      "us_per_launch": round(us, 2), "tflops": round(flops / us / 1e6, 1),
                      "causal_flops": flops, "peak_tflops": peak,
                      "peak_kind": "measured" if pf.exists() else "fallback",
@@ -700,6 +701,8 @@ def main() -> int:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=20.0)
     ap.add_argument("--kernel-case", choices=KERNEL_CASES, help="run one op alone (profiling harness)")
+    ap.add_argument("--prefill-seqs", type=int, default=8, help="prefill_attention case: sequences")
+    ap.add_argument("--prefill-len", type=int, default=560, help="prefill_attention case: tokens per sequence")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
