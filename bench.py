@@ -671,6 +671,38 @@ def package_load_case(args, torch, device) -> dict:
             "host_threads": os.cpu_count(), "note": "package files in the page cache (written just before)"}
 
 
+def run_serve(args, torch, rank: int, world: int, device) -> dict | None:
+    """Config 5: 256 requests (513 point-embedding rows + U{47..511} text
+    tokens, outputs U{16, 64, 256}, all at t = 0) routed over the replicas
+    (one per GPU, data parallel), each served by continuous batching
+    (nanopointllm_b200.serving); output tokens/s of the whole job over the
+    slowest replica's time."""
+    from nanopointllm_b200 import runner as R, serving as SV, synthetic as S
+    shape = S.LLAMA_7B if args.layers == 32 else S.LlamaShape(**{**S.LLAMA_7B.as_dict(), "layers": args.layers})
+    reqs = SV.config5_requests(args.serve_requests, vocab=shape.vocab)
+    share = SV.route(reqs, world)[rank]
+    max_len = max(q.n_point_rows + len(q.text_ids) + q.max_tokens for q in reqs)
+    max_blocks = -(-max_len // BLOCK_SIZE)
+    num_blocks = args.serve_max_seqs * max_blocks + 8
+    run = R.W8A8LlamaRunner(shape, S.LazyLlamaWeights(shape, seed=rank_seed(rank), device=str(device)),
+                            device=device, num_blocks=num_blocks, block_size=BLOCK_SIZE)
+    eng = SV.ServingEngine(run, max_num_seqs=args.serve_max_seqs, max_num_batched_tokens=16384,
+                           max_blocks_per_seq=max_blocks)
+    res = eng.run(share)
+    out = SV.gather_metrics(res) if world > 1 else SV.gather_metrics_local(res)
+    if rank != 0:
+        return None
+    return {"metric": "config5 serving output tokens/s (continuous batching, greedy)",
+            "value": round(out["output_tokens_per_s"], 1), "unit": "tokens/s", "n_gpus": world,
+            "higher_is_better": True, "scaling": "strong", "dtype": "int8 (W8A8), fp16 attention",
+            "data": "synthetic", "config": {"workload": f"config5: {len(reqs)} requests, 513 point rows + "
+                                                        "U{47..511} text tokens, outputs U{16,64,256}",
+                                            "parallelism": f"dp{world}", "max_num_seqs": args.serve_max_seqs,
+                                            "block_size": BLOCK_SIZE},
+            "serving": {k: (round(v, 4) if isinstance(v, float) else v) for k, v in out.items()},
+            "steps": res["steps"]}
+
+
 def run_reference(args, rank: int) -> dict | None:
     if rank != 0:
         return None
@@ -701,6 +733,9 @@ def main() -> int:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=20.0)
     ap.add_argument("--kernel-case", choices=KERNEL_CASES, help="run one op alone (profiling harness)")
+    ap.add_argument("--serve", action="store_true", help="config 5 serving run instead of the decode metric")
+    ap.add_argument("--serve-requests", type=int, default=256)
+    ap.add_argument("--serve-max-seqs", type=int, default=64)
     ap.add_argument("--prefill-seqs", type=int, default=8, help="prefill_attention case: sequences")
     ap.add_argument("--prefill-len", type=int, default=560, help="prefill_attention case: tokens per sequence")
     args = ap.parse_args()
@@ -729,7 +764,8 @@ def main() -> int:
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
     try:
-        line = run_ours(args, torch, dist, rank, world, device)
+        line = run_serve(args, torch, rank, world, device) if args.serve else \
+            run_ours(args, torch, dist, rank, world, device)
     finally:
         if dist is not None:
             dist.destroy_process_group()

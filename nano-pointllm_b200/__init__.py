@@ -15,6 +15,9 @@ Public surface, mirroring the reference ``nanopointllm`` API for this path:
 * ``nanopointllm_b200.tp``              - the same runner split over GPUs
   (tensor parallel: column-parallel QKV / gate-up / LM head, row-parallel
   O / down with int32 all-reduce)
+* ``nanopointllm_b200.serving``         - continuous-batching driver (block
+  manager, FIFO two-queue scheduler, mixed prefill/decode steps, per-bucket
+  decode graphs) and the data-parallel request router across replicas
 * ``nanopointllm_b200.package``         - checksummed int8 packages: the
   reference's single-linear package schema and a whole-model package the
   runners start from without re-quantising (``W8A8LlamaRunner.from_package``)
@@ -24,4 +27,4 @@ from ``csrc/``; there is no CPU or library fallback.
 """
 from __future__ import annotations
 
-__all__ = ["w8a8", "paged_attention", "runner", "synthetic", "tp", "package"]
+__all__ = ["w8a8", "paged_attention", "runner", "synthetic", "tp", "package", "serving"]
