@@ -606,7 +606,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ---------------------------------------------------------- TMA producer
     if (lane == 0) {
-      const uint64_t pol_w = policy_evict_first();
+      // decode tiles read each weight tile once: evict first; prefill tiles
+      // read it once per token tile, so it stays in L2 for the next one
+      const uint64_t pol_w = NT >= 128 ? policy_evict_normal() : policy_evict_first();
       const uint64_t pol_x = policy_evict_last();
       // Weights do not depend on earlier kernels: the weight tiles of the
       // first ring stages are requested before waiting for the previous
