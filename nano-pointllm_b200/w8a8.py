@@ -63,6 +63,8 @@ def dynamic_per_token_quant(values: torch.Tensor, *, out: torch.Tensor | None = 
     rows, k = x.shape
     q = out if out is not None else torch.empty((rows, k), dtype=torch.int8, device=x.device)
     s = scale_out if scale_out is not None else torch.empty((rows,), dtype=torch.float32, device=x.device)
+    if rows == 0:  # nothing to launch (an empty tensor may have no device address)
+        return q.reshape(values.shape), s.reshape(*values.shape[:-1], 1)
     L.check(L.lib.npl_quant_rows(x.data_ptr(), _DT[x.dtype], rows, k, x.stride(0), q.data_ptr(), q.stride(0),
                                  s.data_ptr(), L.stream_ptr(x.device)))
     return q.reshape(values.shape), s.reshape(*values.shape[:-1], 1)
@@ -143,6 +145,8 @@ def linear_q(qa: torch.Tensor, sa: torch.Tensor, qweight: torch.Tensor, wscale: 
     cols = n // 2 if epilogue == L.EPI_SILU_MUL else n
     if out is None:
         out = torch.empty((m, cols), dtype=torch.float16 if epilogue else out_dtype, device=qa.device)
+    if m == 0:  # nothing to launch (an empty tensor may have no device address)
+        return out
     ws = linear_workspace(qa.device, m, n, k)
     res = residual
     L.check(L.lib.npl_w8a8_linear(
