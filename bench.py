@@ -129,13 +129,20 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------- our arm
-def build_runner(torch, shape, steps_total: int, device, seed: int):
+def build_runner(torch, shape, steps_total: int, device, seed: int, tp: bool = False, peer_exchange: bool = True):
+    """The 7B W8A8 runner (tp: the tensor-parallel runner over all ranks of
+    the default process group, every rank building from the same seed)."""
     from nanopointllm_b200 import runner as R
     from nanopointllm_b200 import synthetic as S
+    from nanopointllm_b200 import tp as TP
     blocks_per_seq = (CTX + steps_total + BLOCK_SIZE - 1) // BLOCK_SIZE
     num_blocks = BATCH * blocks_per_seq + 4
     weights = S.LazyLlamaWeights(shape, seed=seed, device=str(device))
-    run = R.W8A8LlamaRunner(shape, weights, device=device, num_blocks=num_blocks, block_size=BLOCK_SIZE)
+    if tp:
+        run = TP.W8A8TPLlamaRunner(shape, weights, device=device, num_blocks=num_blocks, block_size=BLOCK_SIZE,
+                                   peer_exchange=peer_exchange)
+    else:
+        run = R.W8A8LlamaRunner(shape, weights, device=device, num_blocks=num_blocks, block_size=BLOCK_SIZE)
     bt = S.permuted_block_tables(BATCH, blocks_per_seq, num_blocks, seed=seed + 3).to(device)
     return run, bt
 
@@ -222,16 +229,18 @@ def op_bytes(shape, name: str, ctx_len: int, fused_mlp: bool = False) -> int:
     return 0
 
 
-def run_ours(args, torch, dist, rank: int, world: int, device) -> dict | None:
-    from nanopointllm_b200 import _lib, runner as R
+def bench_shape(args):
     from nanopointllm_b200 import synthetic as S
-    shape = S.LLAMA_7B if args.layers == 32 else S.LlamaShape(**{**S.LLAMA_7B.as_dict(), "layers": args.layers})
-    n_eager = 2
-    steps_total = args.warmup + args.steps * 2 + n_eager + 2
-    run, bt = build_runner(torch, shape, steps_total, device, seed=rank_seed(rank))
-    first = prefill(torch, run, bt, device, seed=rank_seed(rank))
-    torch.cuda.synchronize()
+    return S.LLAMA_7B if args.layers == 32 else S.LlamaShape(**{**S.LLAMA_7B.as_dict(), "layers": args.layers})
 
+
+def timed_decode(args, torch, dist, run, bt, first, device, steps_total: int):
+    """Captures the decode graph, runs the warm-up steps, then times
+    args.steps replays on the device (max over ranks) and args.steps replays
+    end to end (pinned host metadata in, greedy tokens out). Returns the
+    graph, the next step index, the device and e2e times (ms), the
+    per-step host<->device bytes and the clock record."""
+    from nanopointllm_b200 import runner as R
     graph = R.DecodeGraph(run, BATCH, bt.shape[1])
     step = 0
     positions, slots, ctx = step_metadata(torch, bt, step, device)
@@ -300,6 +309,19 @@ def run_ours(args, torch, dist, rank: int, world: int, device) -> dict | None:
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(torch, dist, e2.elapsed_time(e3), device)
     step += args.steps
+    return graph, step, meta, dev_ms, e2e_ms, h2d, d2h, clock_info
+
+
+def run_ours(args, torch, dist, rank: int, world: int, device) -> dict | None:
+    from nanopointllm_b200 import _lib, runner as R
+    shape = bench_shape(args)
+    n_eager = 2
+    steps_total = args.warmup + args.steps * 2 + n_eager + 2
+    run, bt = build_runner(torch, shape, steps_total, device, seed=rank_seed(rank))
+    first = prefill(torch, run, bt, device, seed=rank_seed(rank))
+    torch.cuda.synchronize()
+    graph, step, meta, dev_ms, e2e_ms, h2d, d2h, clock_info = timed_decode(args, torch, dist, run, bt, first,
+                                                                           device, steps_total)
 
     # ---- per-kernel device time: a second decode graph whose ops are each
     # bracketed by timing events recorded inside the graph (on the launch
@@ -397,6 +419,51 @@ def run_ours(args, torch, dist, rank: int, world: int, device) -> dict | None:
     if not args.no_cpu_baseline and world == 1:
         line["cpu_baseline"] = cpu_baseline(seconds=args.cpu_seconds)
     return line
+
+
+def run_tp(args, torch, dist, rank: int, world: int, device) -> dict | None:
+    """Config 3 with the tensor-parallel runner: ONE batch of 8 sequences
+    split over the N ranks (heads and intermediate rows per rank, NCCL
+    all-reduces after O and down, all-gathered logits), captured with its
+    collectives in one decode graph per rank. Strong scaling: value =
+    8 * K / max-over-ranks time."""
+    from nanopointllm_b200 import _lib
+    shape = bench_shape(args)
+    steps_total = args.warmup + args.steps * 2 + 2
+    run, bt = build_runner(torch, shape, steps_total, device, seed=0, tp=world > 1,
+                           peer_exchange=not args.tp_nccl)
+    first = prefill(torch, run, bt, device, seed=0)
+    torch.cuda.synchronize()
+    graph, step, meta, dev_ms, e2e_ms, h2d, d2h, clock_info = timed_decode(args, torch, dist, run, bt, first,
+                                                                           device, steps_total)
+    del graph  # releases the NCCL calls captured in it before the process group goes
+    torch.cuda.synchronize()
+    _lib.device_status()
+    if rank != 0:
+        return None
+    tokens = BATCH * args.steps
+    kernels_per_step = shape.layers * 9 + 2  # library kernels; NCCL collectives come on top
+    return {
+        "metric": METRIC, "value": round(tokens / (dev_ms * 1e-3), 2), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dev_ms / args.steps, 4),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "int8 (W8A8: int8 x int8 -> int32, fp16 activations/KV)",
+        "data": "synthetic (random-init 7B weights ~N(0,0.02); 513 point embeddings ~N(0,1) + 511 uniform text ids)",
+        "config": {"workload": "config3 decode step, tensor parallel: batch 8, ctx 1024 (prefilled), block_size "
+                               "256, permuted block table, greedy, CUDA graph with the NCCL collectives",
+                   "batch": BATCH, "context": CTX, "layers": shape.layers, "parallelism": f"tp{world}",
+                   "exchanges_per_layer": ("absmax MAX + int32 SUM all-reduce before O and before down "
+                                           "(4 NCCL all-reduces)" if args.tp_nccl or world == 1 else
+                                           "absmax MAX (fused with the quantisation) and int32 SUM (fused "
+                                           "with the dequant + residual) through NVLink peer memory, before "
+                                           "O and before down (4 exchange kernels)") +
+                                          "; logits all-gather (NCCL) once per step",
+                   "l2": "no flush: each step streams the rank's weight and KV slices (>> 126 MB L2)"},
+        "e2e": {"value": round(tokens / (e2e_ms * 1e-3), 2), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "gpu_launches": kernels_per_step * args.steps,
+        "clocks": clock_info,
+    }
 
 
 def standalone_linears(torch, run, shape, device) -> dict:
@@ -679,17 +746,25 @@ def run_serve(args, torch, rank: int, world: int, device) -> dict | None:
     slowest replica's time."""
     from nanopointllm_b200 import runner as R, serving as SV, synthetic as S
     shape = S.LLAMA_7B if args.layers == 32 else S.LlamaShape(**{**S.LLAMA_7B.as_dict(), "layers": args.layers})
+    from nanopointllm_b200 import tp as TP
     reqs = SV.config5_requests(args.serve_requests, vocab=shape.vocab)
-    share = SV.route(reqs, world)[rank]
+    tp = args.tp and world > 1
+    # data parallel: each replica serves its routed share with its own
+    # weights; tensor parallel: every rank serves all requests in lock step
+    share = reqs if tp else SV.route(reqs, world)[rank]
     max_len = max(q.n_point_rows + len(q.text_ids) + q.max_tokens for q in reqs)
     max_blocks = -(-max_len // BLOCK_SIZE)
     num_blocks = args.serve_max_seqs * max_blocks + 8
-    run = R.W8A8LlamaRunner(shape, S.LazyLlamaWeights(shape, seed=rank_seed(rank), device=str(device)),
-                            device=device, num_blocks=num_blocks, block_size=BLOCK_SIZE)
+    cls = TP.W8A8TPLlamaRunner if tp else R.W8A8LlamaRunner
+    kw = {"peer_exchange": not args.tp_nccl} if tp else {}
+    run = cls(shape, S.LazyLlamaWeights(shape, seed=0 if tp else rank_seed(rank), device=str(device)),
+              device=device, num_blocks=num_blocks, block_size=BLOCK_SIZE, **kw)
     eng = SV.ServingEngine(run, max_num_seqs=args.serve_max_seqs, max_num_batched_tokens=16384,
                            max_blocks_per_seq=max_blocks)
     res = eng.run(share)
-    out = SV.gather_metrics(res) if world > 1 else SV.gather_metrics_local(res)
+    out = SV.gather_metrics(res) if world > 1 and not tp else SV.gather_metrics_local(res)
+    eng.graphs.clear()  # releases the decode graphs (and any NCCL calls in them) before the process group goes
+    torch.cuda.synchronize()
     if rank != 0:
         return None
     return {"metric": "config5 serving output tokens/s (continuous batching, greedy)",
@@ -697,7 +772,8 @@ def run_serve(args, torch, rank: int, world: int, device) -> dict | None:
             "higher_is_better": True, "scaling": "strong", "dtype": "int8 (W8A8), fp16 attention",
             "data": "synthetic", "config": {"workload": f"config5: {len(reqs)} requests, 513 point rows + "
                                                         "U{47..511} text tokens, outputs U{16,64,256}",
-                                            "parallelism": f"dp{world}", "max_num_seqs": args.serve_max_seqs,
+                                            "parallelism": f"tp{world}" if tp else f"dp{world}",
+                                            "max_num_seqs": args.serve_max_seqs,
                                             "block_size": BLOCK_SIZE},
             "serving": {k: (round(v, 4) if isinstance(v, float) else v) for k, v in out.items()},
             "steps": res["steps"]}
@@ -734,6 +810,10 @@ def main() -> int:
     ap.add_argument("--cpu-seconds", type=float, default=20.0)
     ap.add_argument("--kernel-case", choices=KERNEL_CASES, help="run one op alone (profiling harness)")
     ap.add_argument("--serve", action="store_true", help="config 5 serving run instead of the decode metric")
+    ap.add_argument("--tp", action="store_true",
+                    help="tensor parallel over the N ranks (decode step, or --serve) instead of N replicas")
+    ap.add_argument("--tp-nccl", action="store_true",
+                    help="with --tp: NCCL all-reduces instead of the NVLink peer-memory exchanges")
     ap.add_argument("--serve-requests", type=int, default=256)
     ap.add_argument("--serve-max-seqs", type=int, default=64)
     ap.add_argument("--prefill-seqs", type=int, default=8, help="prefill_attention case: sequences")
@@ -764,8 +844,12 @@ def main() -> int:
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
     try:
-        line = run_serve(args, torch, rank, world, device) if args.serve else \
-            run_ours(args, torch, dist, rank, world, device)
+        if args.serve:
+            line = run_serve(args, torch, rank, world, device)
+        elif args.tp:
+            line = run_tp(args, torch, dist, rank, world, device)
+        else:
+            line = run_ours(args, torch, dist, rank, world, device)
     finally:
         if dist is not None:
             dist.destroy_process_group()

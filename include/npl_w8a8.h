@@ -295,6 +295,54 @@ int npl_paged_prefill_attention(const void* q, int ld_q, int total_q, int H, int
                                 const int32_t* q_offsets, int B, int max_q_len, float scale, void* out, int ld_out,
                                 void* stream);
 
+/*
+ * Tensor-parallel exchanges over NVLink peer memory (one process per GPU).
+ * They replace, for decode batches, the NCCL path of a row-parallel linear
+ * (the tensor-parallel variant of the reference's O / down projections,
+ * paged_attention.py:118-124 and lightweight_runner.py:320-383, 539-552):
+ *   npl_row_absmax -> all-reduce(MAX) -> npl_quant_rows_absmax   by npl_tp_absmax_quant
+ *   all-reduce(SUM) of int32 partials -> npl_dequant             by npl_tp_allreduce_dequant
+ * with identical results. Each rank owns one zero-filled exchange buffer of
+ * npl_tp_exchange_bytes(world, max_elems) bytes (256-byte aligned) and maps
+ * every peer's with npl_ipc_handle / npl_ipc_open (CUDA IPC); npl_tp_peers
+ * lists all ranks' buffers as mapped in the calling process (buffers[rank] =
+ * its own). All ranks make the same sequence of calls with the same shapes;
+ * each call pushes this rank's data into every peer's buffer, raises a
+ * per-slice sequence number there and waits (bounded, ~1 s; on expiry
+ * NPL_DEV code 6 in npl_device_status and the output is not written) for
+ * every peer's. No host work per call: capturable in a CUDA graph.
+ * No counterpart in the reference, which runs on one device.
+ */
+#define NPL_TP_MAX_RANKS 8
+#define NPL_IPC_HANDLE_BYTES 64
+typedef struct {
+  int world;
+  int rank;
+  void* buffers[NPL_TP_MAX_RANKS];
+  long long max_elems; /* the largest M * N of npl_tp_allreduce_dequant (multiple of 4) */
+} npl_tp_peers;
+
+size_t npl_tp_exchange_bytes(int world, long long max_elems);
+/* CUDA IPC of a device buffer: the handle (NPL_IPC_HANDLE_BYTES) of the
+ * allocation holding `ptr` and the offset of `ptr` in it; npl_ipc_open maps a
+ * peer's handle into this process (ptr_out = base_out + offset);
+ * npl_ipc_close unmaps base_out. */
+int npl_ipc_handle(const void* ptr, void* handle_out, size_t* offset_out);
+int npl_ipc_open(const void* handle, size_t offset, void** ptr_out, void** base_out);
+int npl_ipc_close(void* base);
+/* x fp16 [M, K] (this rank's columns of each row, row stride ldx), M <= 64:
+ * q int8 [M, K] (row stride ldq) and scale[M] as npl_quant_rows would give
+ * for the whole rows spread over the ranks (the scale from the max over all
+ * ranks' absmax). K % 16 == 0. */
+int npl_tp_absmax_quant(const npl_tp_peers* peers, const void* x, int M, int K, int ldx, int8_t* q, int ldq,
+                        float* scale, void* stream);
+/* acc int32 [M, N] contiguous: this rank's partial accumulators. out fp16
+ * [M, N] = npl_dequant of the sum over all ranks' acc (NPL_EPI_RESIDUAL when
+ * residual is given, else NPL_EPI_NONE). N % 4 == 0, M * N <= max_elems. */
+int npl_tp_allreduce_dequant(const npl_tp_peers* peers, const int32_t* acc, int M, int N, const float* sa,
+                             const float* sw, const float* bias_or_null, const void* residual_or_null, int ld_res,
+                             void* out, int ld_out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -54,6 +54,15 @@ class NplLinearArgs(ctypes.Structure):
                 ("rope", NplRopeKV)]
 
 
+TP_MAX_RANKS = 8
+IPC_HANDLE_BYTES = 64
+
+
+class NplTpPeers(ctypes.Structure):
+    """npl_tp_peers (include/npl_w8a8.h)."""
+    _fields_ = [("world", _I), ("rank", _I), ("buffers", _P * TP_MAX_RANKS), ("max_elems", ctypes.c_longlong)]
+
+
 # name -> (restype, argtypes); mirrors include/npl_w8a8.h
 SIGNATURES = {
     "npl_last_error_string": (ctypes.c_char_p, []),
@@ -73,6 +82,12 @@ SIGNATURES = {
     "npl_decode_attention_workspace_bytes": (_Z, [_I, _I, _I, _I, _I]),
     "npl_paged_decode_attention": (_I, [_P, _I, _I, _I, _I, _P, _P, _I, _I, _P, _I, _I, _P, _F, _P, _P, _P, _P, _Z,
                                         _P]),
+    "npl_tp_exchange_bytes": (_Z, [_I, ctypes.c_longlong]),
+    "npl_ipc_handle": (_I, [_P, _P, ctypes.POINTER(_Z)]),
+    "npl_ipc_open": (_I, [_P, _Z, ctypes.POINTER(_P), ctypes.POINTER(_P)]),
+    "npl_ipc_close": (_I, [_P]),
+    "npl_tp_absmax_quant": (_I, [ctypes.POINTER(NplTpPeers), _P, _I, _I, _I, _P, _I, _P, _P]),
+    "npl_tp_allreduce_dequant": (_I, [ctypes.POINTER(NplTpPeers), _P, _I, _I, _P, _P, _P, _P, _I, _P, _I, _P]),
     "npl_paged_prefill_attention": (_I, [_P, _I, _I, _I, _I, _I, _P, _P, _I, _I, _P, _I, _I, _P, _P, _P, _I, _I, _F,
                                          _P, _I, _P]),
 }

@@ -95,6 +95,7 @@ enum DeviceError : int {
   NPL_DEV_TIMEOUT_EPILOGUE = 3,
   NPL_DEV_TIMEOUT_TEARDOWN = 4,
   NPL_DEV_BAD_INDEX = 5,  // a slot, block-table entry or position outside its table
+  NPL_DEV_TIMEOUT_PEER = 6,  // a tensor-parallel peer did not raise its exchange flag
 };
 
 constexpr float kFp16Tiny = 6.103515625e-05f;  // torch.finfo(torch.float16).tiny = 2^-14

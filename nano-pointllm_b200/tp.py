@@ -25,6 +25,7 @@ embedding are replicated.
 """
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass, replace
 
 import torch
@@ -127,6 +128,75 @@ class W8A8TPLayer:
         self.v_cache = v_cache
 
 
+class PeerExchange:
+    """The NVLink peer-memory exchanges of the row-parallel linears for decode
+    batches (<= 64 tokens): one zero-filled exchange buffer per rank, mapped by
+    every other rank through CUDA IPC (npl_ipc_*). ``absmax_quant`` and
+    ``allreduce_dequant`` give exactly what the NCCL path gives
+    (row_absmax + all-reduce(MAX) + quant_rows_absmax, and all-reduce(SUM) +
+    dequant) in one kernel each. Every rank must make the same calls in the
+    same order."""
+
+    MAX_ROWS = 64
+
+    def __init__(self, group: dist.ProcessGroup, device: torch.device, max_cols: int):
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world > L.TP_MAX_RANKS:
+            raise ValueError(f"at most {L.TP_MAX_RANKS} ranks")
+        self.max_elems = self.MAX_ROWS * (-(-max_cols // 4) * 4)
+        nbytes = int(L.lib.npl_tp_exchange_bytes(self.world, self.max_elems))
+        # 256-byte aligned start: the allocator returns 512-byte aligned blocks
+        self.buf = torch.zeros(nbytes, dtype=torch.uint8, device=device)
+        handle = ctypes.create_string_buffer(L.IPC_HANDLE_BYTES)
+        offset = ctypes.c_size_t(0)
+        with torch.cuda.device(device):
+            L.check(L.lib.npl_ipc_handle(self.buf.data_ptr(), handle, ctypes.byref(offset)))
+        torch.cuda.synchronize(device)
+        handles: list = [None] * self.world
+        dist.all_gather_object(handles, (handle.raw, offset.value), group=group)
+        self._opened: list[int] = []
+        ptrs = []
+        with torch.cuda.device(device):
+            for r, (h, off) in enumerate(handles):
+                if r == self.rank:
+                    ptrs.append(self.buf.data_ptr())
+                    continue
+                p_out, b_out = ctypes.c_void_p(), ctypes.c_void_p()
+                L.check(L.lib.npl_ipc_open(h, off, ctypes.byref(p_out), ctypes.byref(b_out)))
+                self._opened.append(b_out.value)
+                ptrs.append(p_out.value)
+        self.peers = L.NplTpPeers(self.world, self.rank, (ctypes.c_void_p * L.TP_MAX_RANKS)(*ptrs),
+                                  self.max_elems)
+        dist.barrier(group=group)  # every buffer is zero and mapped before the first push
+
+    def usable(self, m: int, n: int) -> bool:
+        return 0 < m <= self.MAX_ROWS and m * n <= self.max_elems and n % 4 == 0
+
+    def absmax_quant(self, x16: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        m, k = x16.shape
+        q = torch.empty((m, k), dtype=torch.int8, device=x16.device)
+        s = torch.empty((m,), dtype=torch.float32, device=x16.device)
+        L.check(L.lib.npl_tp_absmax_quant(ctypes.byref(self.peers), x16.data_ptr(), m, k, x16.stride(0),
+                                          q.data_ptr(), q.stride(0), s.data_ptr(), L.stream_ptr(x16.device)))
+        return q, s
+
+    def allreduce_dequant(self, acc: torch.Tensor, sa: torch.Tensor, wscale: torch.Tensor,
+                          residual: torch.Tensor | None) -> torch.Tensor:
+        m, n = acc.shape
+        out = torch.empty((m, n), dtype=torch.float16, device=acc.device)
+        L.check(L.lib.npl_tp_allreduce_dequant(
+            ctypes.byref(self.peers), acc.data_ptr(), m, n, sa.data_ptr(), wscale.data_ptr(), None,
+            L.ptr(residual), 0 if residual is None else residual.stride(0), out.data_ptr(), out.stride(0),
+            L.stream_ptr(acc.device)))
+        return out
+
+    def close(self) -> None:
+        for b in self._opened:
+            L.lib.npl_ipc_close(b)
+        self._opened = []
+
+
 class W8A8TPLlamaRunner(W8A8LlamaRunner):
     """W8A8LlamaRunner split over the ranks of `group` (one GPU each). The
     calling convention is the same (forward reads the ForwardContext and
@@ -135,7 +205,11 @@ class W8A8TPLlamaRunner(W8A8LlamaRunner):
 
     def __init__(self, shape: LlamaShape, state_dict: dict[str, torch.Tensor], *, device: torch.device,
                  group: dist.ProcessGroup | None = None, num_blocks: int = 0, block_size: int = 256,
-                 kv_pool: torch.Tensor | None = None):
+                 kv_pool: torch.Tensor | None = None, peer_exchange: bool = True):
+        """``peer_exchange``: decode batches (<= 64 tokens) exchange the
+        row-parallel absmax and int32 partials through NVLink peer memory
+        (PeerExchange) instead of NCCL all-reduces; larger batches use NCCL.
+        Results are identical either way."""
         self.group = group if group is not None else dist.group.WORLD
         self.plan = tp_plan(shape, dist.get_rank(self.group), dist.get_world_size(self.group))
         self.full_shape = shape
@@ -163,6 +237,8 @@ class W8A8TPLlamaRunner(W8A8LlamaRunner):
                                                                                  ZERO_ROW_SCALE))
         self.cos, self.sin = rope_tables(shape.head_dim, shape.max_position, shape.rope_theta, self.device)
         self.scale = shape.head_dim ** -0.5
+        self.xchg = PeerExchange(self.group, self.device, shape.hidden) \
+            if peer_exchange and self.plan.world > 1 else None
 
     # --------------------------------------------------------- exchanges
     def _allreduce(self, t: torch.Tensor, op) -> torch.Tensor:
@@ -172,6 +248,13 @@ class W8A8TPLlamaRunner(W8A8LlamaRunner):
     def _row_parallel(self, x16: torch.Tensor, lin: W.W8A8Linear, residual: torch.Tensor) -> torch.Tensor:
         """fp16 rows [T, K/P] (this rank's part of each row) -> fp16
         residual + x @ W^T over the whole K."""
+        x = self.xchg
+        if x is not None and x.usable(x16.shape[0], lin.out_features):
+            xq, xs = x.absmax_quant(x16)
+            acc = torch.empty((x16.shape[0], lin.out_features), dtype=torch.int32, device=x16.device)
+            scratch = torch.empty((x16.shape[0], lin.out_features), dtype=torch.float16, device=x16.device)
+            W.linear_q(xq, xs, lin.qweight, lin.wscale, out=scratch, acc_out=acc)
+            return x.allreduce_dequant(acc, xs, lin.wscale, residual)
         amax = self._allreduce(W.row_absmax(x16), dist.ReduceOp.MAX)  # whole-row absmax (fp32 bits)
         xq, xs = W.quant_rows_absmax(x16, amax)
         acc = torch.empty((x16.shape[0], lin.out_features), dtype=torch.int32, device=x16.device)

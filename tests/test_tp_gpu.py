@@ -41,11 +41,17 @@ def _rank_main(rank: int, world: int, port: int, pkg_dir: str, errors) -> None:
         bt = S.permuted_block_tables(len(lengths), per_seq, len(lengths) * per_seq, seed=3).numpy()
         full = R.W8A8LlamaRunner(shape, sd, device=dev, num_blocks=len(lengths) * per_seq, block_size=bs)
         t_ref, l_ref = _generate(full, prompts, bt, 5, dev)
-        for graph in (False, True):
-            run = TP.W8A8TPLlamaRunner(shape, sd, device=dev, num_blocks=len(lengths) * per_seq, block_size=bs)
+        # decode steps through the NVLink peer-memory exchanges (eager and
+        # graph), and through the NCCL all-reduces
+        for graph, peer in ((False, True), (True, True), (True, False)):
+            run = TP.W8A8TPLlamaRunner(shape, sd, device=dev, num_blocks=len(lengths) * per_seq, block_size=bs,
+                                       peer_exchange=peer)
+            assert (run.xchg is not None) == peer
             t_tp, l_tp = _generate(run, prompts, bt, 5, dev, graph=graph)
             np.testing.assert_array_equal(t_tp, t_ref)
             np.testing.assert_array_equal(l_tp, l_ref)
+            if run.xchg is not None:
+                run.xchg.close()
             del run
         run = TP.W8A8TPLlamaRunner.from_package(pkg_dir, device=dev, num_blocks=len(lengths) * per_seq,
                                                 block_size=bs)
