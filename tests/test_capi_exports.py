@@ -67,3 +67,18 @@ def test_struct_layout_matches_header(tmp_path):
     got = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split()
     assert [int(v) for v in got] == [ctypes.sizeof(_lib.NplLinearArgs), ctypes.sizeof(_lib.NplRopeKV),
                                      _lib.NplLinearArgs.rope.offset, _lib.NplLinearArgs.absmax_out.offset]
+
+
+def test_tp_exchange_layout_is_host_only():
+    """npl_tp_exchange_bytes: flag and call-count words, then two parities of
+    every rank's int32 slot (max_elems) and absmax slot (64 rows)."""
+    import ctypes as C
+    from nanopointllm_b200 import _lib
+    al = lambda x: (x + 255) & ~255  # noqa: E731
+    for world, max_elems in ((2, 64 * 4096), (8, 64 * 4096), (4, 1024)):
+        head = al(4 * 8 * 64) * 2 + al(4 * 64) * 2
+        want = head + al(4 * 2 * world * max_elems) + al(4 * 2 * world * 64)
+        assert _lib.lib.npl_tp_exchange_bytes(world, max_elems) == want
+    assert _lib.lib.npl_tp_exchange_bytes(9, 1024) == 0      # more ranks than NPL_TP_MAX_RANKS
+    assert _lib.lib.npl_tp_exchange_bytes(2, 1022) == 0      # max_elems not a multiple of 4
+    assert C.sizeof(_lib.NplTpPeers) == 4 + 4 + 8 * _lib.TP_MAX_RANKS + 8
