@@ -776,7 +776,7 @@ def run_serve(args, torch, rank: int, world: int, device) -> dict | None:
                                             "max_num_seqs": args.serve_max_seqs,
                                             "block_size": BLOCK_SIZE},
             "serving": {k: (round(v, 4) if isinstance(v, float) else v) for k, v in out.items()},
-            "steps": res["steps"]}
+            "steps": res["steps"], "step_wall_s": res["step_s"]}
 
 
 def run_reference(args, rank: int) -> dict | None:

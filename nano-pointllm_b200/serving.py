@@ -221,6 +221,7 @@ class ServingEngine:
         self.graphs: dict[int, object] = {}
         self.point_rows_fn = point_rows_fn or self._default_point_rows
         self.steps = {"mixed": 0, "decode": 0}
+        self.step_s = {"mixed": 0.0, "decode": 0.0}  # host wall time per step kind (each step ends synchronised)
 
     def _default_point_rows(self, req: Request) -> torch.Tensor:
         """Seeded N(0, 1) point-feature rows standing in for the point encoder's output."""
@@ -233,12 +234,31 @@ class ServingEngine:
         return [seq.block_table[p // bs] * bs + p % bs for p in positions]
 
     def _block_tables(self, seqs: Seq[Sequence], rows: int) -> torch.Tensor:
-        bt = torch.zeros(rows, self.max_blocks, dtype=torch.int32)
-        for i, s in enumerate(seqs):
-            if len(s.block_table) > self.max_blocks:
-                raise RuntimeError(f"request {s.req.rid} needs more than {self.max_blocks} KV blocks")
-            bt[i, :len(s.block_table)] = torch.tensor(s.block_table, dtype=torch.int32)
-        return bt
+        """int32 [rows, max_blocks] (host): each sequence's blocks, zero-padded;
+        rows past the sequences are zero. Built as one list (a per-element
+        tensor write costs microseconds each on the host)."""
+        w = self.max_blocks
+        table = []
+        for s in seqs:
+            if len(s.block_table) > w:
+                raise RuntimeError(f"request {s.req.rid} needs more than {w} KV blocks")
+            table.append(s.block_table + [0] * (w - len(s.block_table)))
+        table.extend([[0] * w for _ in range(rows - len(seqs))])
+        return torch.tensor(table, dtype=torch.int32).reshape(rows, w)
+
+    def _decode_metadata(self, decode: Seq[Sequence], bucket: int):
+        """Host tensors of a decode step padded to `bucket` rows: token ids,
+        positions, slots (-1 for padding rows), context lengths and block
+        tables (paged_model_runner.py:332-383 prepare_decode)."""
+        pad = bucket - len(decode)
+        bs = self.bm.block_size
+        last = [s.num_tokens - 1 for s in decode]
+        ids = torch.tensor([s.last_token for s in decode] + [0] * pad, dtype=torch.long)
+        pos = torch.tensor(last + [0] * pad, dtype=torch.long)
+        slots = torch.tensor([s.block_table[p // bs] * bs + p % bs for s, p in zip(decode, last)] + [-1] * pad,
+                             dtype=torch.int32)
+        ctx = torch.tensor([p + 1 for p in last] + [0] * pad, dtype=torch.int32)
+        return ids, pos, slots, ctx, self._block_tables(decode, bucket)
 
     def _run_mixed(self, prefill: list[Sequence], decode: list[Sequence]) -> list[int]:
         """Prompts (their whole sequence) and decode rows in one eager forward
@@ -253,8 +273,9 @@ class ServingEngine:
             slots.extend(self._slots(s, range(s.num_tokens)))
             seq_lens.append(s.num_tokens)
             ctx.append(s.num_tokens)
+        if decode:  # one embedding lookup for all decode rows
+            rows.append(F.embedding(torch.tensor([s.last_token for s in decode], device=dev), r.embed))
         for s in decode:
-            rows.append(F.embedding(torch.tensor([s.last_token], device=dev), r.embed))
             positions.append(s.num_tokens - 1)
             slots.extend(self._slots(s, range(s.num_tokens - 1, s.num_tokens)))
             seq_lens.append(1)
@@ -280,16 +301,7 @@ class ServingEngine:
         dg = self.graphs.get(bucket)
         if dg is None:
             dg = self.graphs[bucket] = self.R.DecodeGraph(self.runner, bucket, self.max_blocks)
-        ids = torch.zeros(bucket, dtype=torch.long)
-        pos = torch.zeros(bucket, dtype=torch.long)
-        slots = torch.full((bucket,), -1, dtype=torch.int32)
-        ctx = torch.zeros(bucket, dtype=torch.int32)
-        for i, s in enumerate(decode):
-            ids[i] = s.last_token
-            pos[i] = s.num_tokens - 1
-            slots[i] = self._slots(s, range(s.num_tokens - 1, s.num_tokens))[0]
-            ctx[i] = s.num_tokens
-        bt = self._block_tables(decode, bucket)
+        ids, pos, slots, ctx, bt = self._decode_metadata(decode, bucket)
         if dg.graph is None:
             dg.load(ids, pos, slots, ctx, bt, non_blocking=False)
             dg.capture()  # runs the step twice eagerly: the KV writes are the same values
@@ -303,8 +315,11 @@ class ServingEngine:
             if self.sched.waiting:
                 raise RuntimeError("a waiting request does not fit in the KV pool")
             return []
+        t0 = time.perf_counter()
         tokens = self._run_mixed(prefill, decode) if prefill else self._run_decode(decode)
-        return self.sched.postprocess(prefill + decode, tokens, time.perf_counter())
+        now = time.perf_counter()
+        self.step_s["mixed" if prefill else "decode"] += now - t0
+        return self.sched.postprocess(prefill + decode, tokens, now)
 
     def run(self, requests: Seq[Request]) -> dict:
         """Serves every request; returns per-request outputs and timings."""
@@ -327,6 +342,7 @@ class ServingEngine:
             "prompt_tokens": sum(s.num_prompt_tokens for s in seqs),
             "preemptions": sum(s.preemptions for s in seqs),
             "steps": dict(self.steps),
+            "step_s": {k: round(v, 4) for k, v in self.step_s.items()},
         }
 
 

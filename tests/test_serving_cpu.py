@@ -151,3 +151,36 @@ def test_gather_metrics_world2():
     while not errors.empty():
         msgs.append(errors.get())
     assert not alive and not msgs, "\n".join(msgs)
+
+
+def test_decode_metadata_rows_and_padding():
+    """The host metadata of a padded decode step: per sequence its last
+    token, position, KV slot and context length, its block table zero-padded;
+    padding rows at slot -1 and context 0."""
+    S = _S()
+
+    class _Runner:  # what ServingEngine reads from its runner on the host
+        num_blocks, block_size, device = 32, 4, "cpu"
+
+    eng = S.ServingEngine(_Runner(), max_num_seqs=4, max_blocks_per_seq=5)
+    seqs = []
+    for rid, (n_text, n_pts) in enumerate([(3, 2), (9, 0), (1, 6)]):
+        s = S.Sequence(S.Request(rid=rid, text_ids=list(range(10 + rid, 10 + rid + n_text)), max_tokens=4,
+                                 n_point_rows=n_pts))
+        eng.bm.allocate(s)
+        s.token_ids.append(100 + rid)  # one generated token: its KV is written by this step
+        eng.bm.may_append(s)
+        seqs.append(s)
+    ids, pos, slots, ctx, bt = eng._decode_metadata(seqs, 8)
+    assert ids.tolist() == [100, 101, 102] + [0] * 5
+    assert pos.tolist() == [s.num_tokens - 1 for s in seqs] + [0] * 5
+    want_slots = [s.block_table[(s.num_tokens - 1) // 4] * 4 + (s.num_tokens - 1) % 4 for s in seqs]
+    assert slots.tolist() == want_slots + [-1] * 5
+    assert ctx.tolist() == [s.num_tokens for s in seqs] + [0] * 5
+    assert bt.shape == (8, 5) and bt.dtype.is_floating_point is False
+    for i, s in enumerate(seqs):
+        assert bt[i].tolist() == s.block_table + [0] * (5 - len(s.block_table))
+    assert bt[3:].abs().sum().item() == 0
+    seqs[0].block_table += [1, 2, 3, 4]  # more blocks than a row holds
+    with pytest.raises(RuntimeError):
+        eng._block_tables(seqs, 4)
