@@ -50,8 +50,11 @@ __global__ void store_kv_kernel(const __half* __restrict__ key, const __half* __
 }
 
 // -------------------------------------------------------- RoPE + store
-// Grid (token, head of q | k | v), D/2 threads. Pair (d, d + D/2) of a q/k
-// head:
+// Grid (token, group of `hpc` heads of q | k | v); the CTA's threads walk the
+// (head, d) pairs of its group. Decode batches take one head per CTA and D/2
+// threads (many small CTAs in parallel); prefill batches take every head of a
+// token in one CTA (a CTA per (token, head) made ~10^6 tiny CTAs, bound by
+// CTA launch). Pair (d, d + D/2) of a q/k head:
 //   out[d]       = fp16(fp16(x1 * cos[d])       + fp16(-x2 * sin[d]))
 //   out[d + D/2] = fp16(fp16(x2 * cos[d + D/2]) + fp16( x1 * sin[d + D/2]))
 // (HF apply_rotary_pos_emb with rotate_half(x) = cat(-x2, x1), each torch
@@ -61,45 +64,49 @@ __global__ void rope_store_kernel(const __half* __restrict__ qkv, int ld_qkv, in
                                   int max_position, const int64_t* __restrict__ positions,
                                   const int32_t* __restrict__ slots, __half* __restrict__ q_out,
                                   __half* __restrict__ kc, __half* __restrict__ vc, long long num_slots,
-                                  int* status) {
+                                  int hpc, int* status) {
   pdl_wait();
   pdl_trigger();
-  const int t = blockIdx.x, head = blockIdx.y, d = threadIdx.x;
+  const int t = blockIdx.x, head0 = blockIdx.y * hpc;
   const int half_d = D / 2;
   const long long pos = positions[t];
   const long long slot = slots[t];
   const bool pos_ok = pos >= 0 && pos < max_position;
   const bool slot_ok = slot >= 0 && slot < num_slots;
-  if (head == 0 && d == 0 && (!pos_ok || slot >= num_slots)) flag_bad_index(status);
-  const __half* x = qkv + (size_t)t * ld_qkv + (size_t)head * D;
-  if (head >= H + Hkv) {  // v
-    if (slot_ok) {
-      __half* vd = vc + (slot * Hkv + (head - H - Hkv)) * D;
-      vd[d] = x[d];
-      vd[d + half_d] = x[d + half_d];
+  if (head0 == 0 && threadIdx.x == 0 && (!pos_ok || slot >= num_slots)) flag_bad_index(status);
+  const int heads = min(hpc, H + 2 * Hkv - head0);
+  for (int i = threadIdx.x; i < heads * half_d; i += blockDim.x) {
+    const int head = head0 + i / half_d, d = i % half_d;
+    const __half* x = qkv + (size_t)t * ld_qkv + (size_t)head * D;
+    if (head >= H + Hkv) {  // v
+      if (slot_ok) {
+        __half* vd = vc + (slot * Hkv + (head - H - Hkv)) * D;
+        vd[d] = x[d];
+        vd[d + half_d] = x[d + half_d];
+      }
+      continue;
     }
-    return;
+    if (!pos_ok) continue;
+    const __half* c = cos_t + pos * D;
+    const __half* s = sin_t + pos * D;
+    const float x1 = __half2float(x[d]);
+    const float x2 = __half2float(x[d + half_d]);
+    const float a1 = __half2float(__float2half_rn(__fmul_rn(x1, __half2float(c[d]))));
+    const float b1 = __half2float(__float2half_rn(__fmul_rn(-x2, __half2float(s[d]))));
+    const float a2 = __half2float(__float2half_rn(__fmul_rn(x2, __half2float(c[d + half_d]))));
+    const float b2 = __half2float(__float2half_rn(__fmul_rn(x1, __half2float(s[d + half_d]))));
+    const __half o1 = __float2half_rn(__fadd_rn(a1, b1));
+    const __half o2 = __float2half_rn(__fadd_rn(a2, b2));
+    __half* dst;
+    if (head < H) {
+      dst = q_out + ((size_t)t * H + head) * D;
+    } else {
+      if (!slot_ok) continue;
+      dst = kc + (slot * Hkv + (head - H)) * D;
+    }
+    dst[d] = o1;
+    dst[d + half_d] = o2;
   }
-  if (!pos_ok) return;
-  const __half* c = cos_t + pos * D;
-  const __half* s = sin_t + pos * D;
-  const float x1 = __half2float(x[d]);
-  const float x2 = __half2float(x[d + half_d]);
-  const float a1 = __half2float(__float2half_rn(__fmul_rn(x1, __half2float(c[d]))));
-  const float b1 = __half2float(__float2half_rn(__fmul_rn(-x2, __half2float(s[d]))));
-  const float a2 = __half2float(__float2half_rn(__fmul_rn(x2, __half2float(c[d + half_d]))));
-  const float b2 = __half2float(__float2half_rn(__fmul_rn(x1, __half2float(s[d + half_d]))));
-  const __half o1 = __float2half_rn(__fadd_rn(a1, b1));
-  const __half o2 = __float2half_rn(__fadd_rn(a2, b2));
-  __half* dst;
-  if (head < H) {
-    dst = q_out + ((size_t)t * H + head) * D;
-  } else {
-    if (!slot_ok) return;
-    dst = kc + (slot * Hkv + (head - H)) * D;
-  }
-  dst[d] = o1;
-  dst[d + half_d] = o2;
 }
 
 // ------------------------------------------------- paged decode attention
@@ -595,11 +602,15 @@ extern "C" int npl_rope_store_kv(const void* qkv, int ld_qkv, int T, int H, int 
       max_position <= 0 || num_blocks <= 0 || block_size <= 0)
     return fail(NPL_ERR_ARG, "npl_rope_store_kv: bad shape");
   if (T == 0) return NPL_OK;
-  return launch_pdl("npl_rope_store_kv", rope_store_kernel, dim3(T, H + 2 * Hkv), dim3(D / 2), 0,
+  // decode batches: one head per CTA; larger batches: every head of a token
+  const int all_heads = H + 2 * Hkv;
+  const int hpc = T <= 64 ? 1 : all_heads;
+  const int threads = T <= 64 ? D / 2 : std::min(512, ((all_heads * D / 2 + 31) / 32) * 32);
+  return launch_pdl("npl_rope_store_kv", rope_store_kernel, dim3(T, (all_heads + hpc - 1) / hpc), dim3(threads), 0,
                     static_cast<cudaStream_t>(stream), static_cast<const __half*>(qkv), ld_qkv, H, Hkv, D,
                     static_cast<const __half*>(cos_table), static_cast<const __half*>(sin_table), max_position,
                     positions, slot_mapping, static_cast<__half*>(q_out), static_cast<__half*>(k_cache),
-                    static_cast<__half*>(v_cache), (long long)num_blocks * block_size, device_status_ptr());
+                    static_cast<__half*>(v_cache), (long long)num_blocks * block_size, hpc, device_status_ptr());
 }
 
 extern "C" size_t npl_decode_attention_workspace_bytes(int B, int H, int D, int max_blocks, int block_size) {

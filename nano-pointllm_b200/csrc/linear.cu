@@ -351,6 +351,68 @@ __device__ __forceinline__ void epilogue_chunk(const LinearArgs& p, LinearCtl& c
   }
 }
 
+// Residual epilogue of 8 token columns [c0, c0 + 8) of tile row `row`, with
+// the chunk's residuals already in registers: out = fp16(fp16(v) + res).
+template <int NT>
+__device__ __forceinline__ void residual_chunk(const LinearArgs& p, const float* sa, int m_tile, int n_tile, int row,
+                                               int c0, const int32_t (&acc)[8], const EpiOperands& e,
+                                               const __half* res8) {
+  const int n = n_tile * kTileN + row;
+  const int m_base = m_tile * NT + c0;
+  if (p.acc_out && n < p.N) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (m_base + j < p.M) p.acc_out[(size_t)(m_base + j) * p.N + n] = acc[j];
+  }
+  if (n >= p.N) return;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int m = m_base + j;
+    if (m >= p.M) break;
+    const float o = __half2float(__float2half_rn(dequant(acc[j], sa[m], e.sw, p.bias, e.bias)));
+    static_cast<__half*>(p.out)[(size_t)m * p.ld_out + n] = __float2half_rn(__fadd_rn(o, __half2float(res8[j])));
+  }
+}
+
+// Epilogue of a whole token tile, 8 token columns at a time; get_acc(c0, acc)
+// yields the accumulators of columns [c0, c0 + 8). The residual epilogue
+// loads the residuals of up to 32 tokens together before their chunks run
+// (the first 8 were loaded before the accumulator was ready), so a 256-token
+// prefill tile costs 8 residual round trips instead of 32. The other
+// epilogues keep a compact loop.
+template <int NT, typename AccFn>
+__device__ __forceinline__ void epilogue_tile(const LinearArgs& p, LinearCtl& c, const float* sa, int m_tile,
+                                              int n_tile, int row, const EpiOperands& e, AccFn&& get_acc) {
+  if (p.epilogue != NPL_EPI_RESIDUAL) {
+    for (int c0 = 0; c0 < NT; c0 += 8) {
+      int32_t acc[8];
+      get_acc(c0, acc);
+      epilogue_chunk<NT>(p, c, sa, m_tile, n_tile, row, c0, acc, e);
+    }
+    return;
+  }
+  constexpr int G = NT < 32 ? NT : 32;
+  const int n = n_tile * kTileN + row;
+  for (int g0 = 0; g0 < NT; g0 += G) {
+    __half res[G];
+#pragma unroll
+    for (int j = 0; j < G; ++j) {
+      if (g0 == 0 && j < 8) {
+        res[j] = e.res[j];
+      } else {
+        const int m = m_tile * NT + g0 + j;
+        res[j] = (m < p.M && n < p.N) ? p.residual[(size_t)m * p.ld_res + n] : __float2half_rn(0.f);
+      }
+    }
+#pragma unroll
+    for (int cc = 0; cc < G; cc += 8) {
+      int32_t acc[8];
+      get_acc(g0 + cc, acc);
+      residual_chunk<NT>(p, sa, m_tile, n_tile, row, g0 + cc, acc, e, res + cc);
+    }
+  }
+}
+
 __device__ __forceinline__ void unpack_f16x8(const uint4& x, float (&v)[8]) {
   const __half2* h = reinterpret_cast<const __half2*>(&x);
 #pragma unroll
@@ -767,8 +829,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (leader) {
           if (ct == 0) mbar_arrive_expect_tx(&c.rfull[rb], (uint32_t)(p.split - 1) * red_bytes);
           mbar_wait_cluster(&c.rfull[rb], use & 1, p.status, NPL_DEV_TIMEOUT_EPILOGUE);
-          for (int c0 = 0; c0 < NT; c0 += 8) {
-            int32_t acc[8];
+          epilogue_tile<NT>(p, c, sa, m_tile, n_tile, row, eo, [&](int c0, int32_t(&acc)[8]) {
             tmem_ld_x8(taddr + c0, acc);
             tmem_wait_ld();
 #pragma unroll
@@ -777,8 +838,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               acc[j] += *cell;  // int32 sums are exact in any order
               *cell = 0;
             }
-            epilogue_chunk<NT>(p, c, sa, m_tile, n_tile, row, c0, acc, eo);
-          }
+          });
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&c.tempty[buf]);
@@ -812,12 +872,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int slot = (int)(((first_unit + 1) * gridDim.x + p.total_units - 1) / p.total_units) - 1;
       int32_t* ws = p.ws_acc + (size_t)slot * NT * kTileN;
       if (whole) {
-        for (int c0 = 0; c0 < NT; c0 += 8) {
-          int32_t acc[8];
+        epilogue_tile<NT>(p, c, sa, m_tile, n_tile, row, eo, [&](int c0, int32_t(&acc)[8]) {
           tmem_ld_x8(taddr + c0, acc);
           tmem_wait_ld();
-          epilogue_chunk<NT>(p, c, sa, m_tile, n_tile, row, c0, acc, eo);
-        }
+        });
       } else {
         for (int c0 = 0; c0 < NT; c0 += 8) {
           int32_t acc[8];
@@ -837,16 +895,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (ct == 0) c.last_flag = (atomic_add_acq_rel(p.ws_cnt + slot, kb1 - kb0) + (kb1 - kb0) == p.k_blocks);
         epi_bar();
         if (c.last_flag) {
-          for (int c0 = 0; c0 < NT; c0 += 8) {
-            int32_t acc[8];
+          epilogue_tile<NT>(p, c, sa, m_tile, n_tile, row, eo, [&](int c0, int32_t(&acc)[8]) {
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
               int32_t* cell = ws + (size_t)(c0 + j) * kTileN + row;
               acc[j] = __ldcg(cell);
               __stcg(cell, 0);
             }
-            epilogue_chunk<NT>(p, c, sa, m_tile, n_tile, row, c0, acc, eo);
-          }
+          });
           if (ct == 0) p.ws_cnt[slot] = 0;
         }
         epi_bar();

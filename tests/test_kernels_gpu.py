@@ -182,7 +182,8 @@ def test_linear_accumulators_and_dequant_bit_exact(K, m, n, k):
     np.testing.assert_array_equal(cpu(out), O.dequantize(acc, sa, sw, bias))
 
 
-@pytest.mark.parametrize("m,n,k", [(1, 4096, 4096), (8, 4096, 4096), (8, 4096, 11008), (64, 512, 1024), (5, 384, 256)])
+@pytest.mark.parametrize("m,n,k", [(1, 4096, 4096), (8, 4096, 4096), (8, 4096, 11008), (64, 512, 1024), (5, 384, 256),
+                                   (300, 640, 512), (1100, 256, 256)])  # prefill tiles, ragged last tile
 def test_linear_residual_epilogue(K, m, n, k):
     gen = torch.Generator().manual_seed(m + n + k + 1)
     qa, qw = _rand_q(gen, m, k), _rand_q(gen, n, k)
@@ -196,7 +197,8 @@ def test_linear_residual_epilogue(K, m, n, k):
     np.testing.assert_array_equal(cpu(out), ref)
 
 
-@pytest.mark.parametrize("m,inter,k", [(1, 11008, 4096), (8, 11008, 4096), (64, 1024, 512), (5, 128, 256)])
+@pytest.mark.parametrize("m,inter,k", [(1, 11008, 4096), (8, 11008, 4096), (64, 1024, 512), (5, 128, 256),
+                                       (300, 1024, 512)])
 def test_linear_silu_mul_epilogue(K, m, inter, k):
     gen = torch.Generator().manual_seed(m + inter + k)
     qa = _rand_q(gen, m, k)
