@@ -34,7 +34,8 @@ peak the prefill roofline is reported against), prefill_attention (the
 varlen prefill attention at config 4: 8 x 560 tokens, causal FLOP/s against
 the measured dense fp16/bf16 peak), package_load (start-up of
 a 7B-geometry runner with ``--layers`` layers from fp16 host weights against
-from the checksummed int8 package).
+from the checksummed int8 package), prefill_forward (one eager prefill
+forward over ``--prefill-seqs`` x ``--prefill-len`` tokens, whole and per op).
 
 ``--impl reference`` times the reference's CPU W8A8 path on the host cores:
 the numpy port of the reference algorithm in oracle/ (the reference itself is
@@ -568,7 +569,7 @@ def cpu_baseline(seconds: float = 20.0) -> dict:
 
 # ------------------------------------------------------- single-op cases
 KERNEL_CASES = ("qkv", "o", "gate_up", "down", "lm_head", "attention", "rmsnorm_quant", "prefill", "int8_peak",
-                "prefill_attention", "package_load")
+                "prefill_attention", "package_load", "prefill_forward")
 
 
 def run_kernel_case(args, torch, device) -> dict:
@@ -691,8 +692,73 @@ def run_kernel_case(args, torch, device) -> dict:
                      "frac": round(flops / us / 1e6 / peak, 3)})
     elif name == "package_load":
         line.update(package_load_case(args, torch, device))
+    elif name == "prefill_forward":
+        line.update(prefill_forward_case(args, torch, device))
     L.device_status()
     return line
+
+
+def prefill_forward_case(args, torch, device) -> dict:
+    """One eager prefill forward of the 7B W8A8 runner (``--layers`` layers)
+    over ``--prefill-seqs`` x ``--prefill-len`` tokens (the first mixed step
+    of config-5 serving admits ~20 x 800): device time of the whole forward,
+    then of every op bracketed by CUDA events (which stops programmatic
+    dependent launch overlap, so the sum is slightly larger)."""
+    import collections
+    from nanopointllm_b200 import runner as R, synthetic as S
+    shape = bench_shape(args)
+    n_seq, t = args.prefill_seqs, args.prefill_len
+    per = -(-t // BLOCK_SIZE)
+    nb = n_seq * per + 4
+    run = R.W8A8LlamaRunner(shape, S.LazyLlamaWeights(shape, seed=0, device=str(device)), device=device,
+                            num_blocks=nb, block_size=BLOCK_SIZE)
+    bt = S.permuted_block_tables(n_seq, per, nb, seed=3).to(device)
+    g = torch.Generator(device=device).manual_seed(0)
+    emb = torch.randn(n_seq * t, shape.hidden, generator=g, device=device).half()
+    pos = torch.arange(t, device=device).repeat(n_seq)
+    blk, off = torch.arange(t, device=device) // BLOCK_SIZE, torch.arange(t, device=device) % BLOCK_SIZE
+    slots = (bt[:, blk].long() * BLOCK_SIZE + off).reshape(-1).to(torch.int32)
+    ctx_lens = torch.full((n_seq,), t, dtype=torch.int32, device=device)
+
+    def forward():
+        R.set_forward_context(R.ForwardContext(slot_mapping=slots, block_tables=bt, context_lens=ctx_lens,
+                                               position_ids=pos, seq_lens=[t] * n_seq))
+        try:
+            return run.forward(inputs_embeds=emb, position_ids=pos, last_only=True)
+        finally:
+            R.clear_forward_context()
+
+    for _ in range(args.warmup):
+        forward()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(args.steps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        forward()
+        e1.record()
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1))
+    records = []
+
+    def timer(name, fn, *a, **kw):
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        out = fn(*a, **kw)
+        s1.record()
+        records.append((name, s0, s1))
+        return out
+
+    run.timer = timer
+    forward()
+    run.timer = None
+    torch.cuda.synchronize()
+    per_op: dict[str, float] = collections.OrderedDict()
+    for n, a, b in records:
+        per_op[n] = per_op.get(n, 0.0) + a.elapsed_time(b)
+    return {"kernel": "whole prefill forward (eager)", "config": f"{n_seq} x {t} tokens, {shape.layers} layers",
+            "ms_per_forward": round(statistics.median(times), 2),
+            "per_op_ms": {k: round(v, 2) for k, v in per_op.items()}}
 
 
 def package_load_case(args, torch, device) -> dict:
