@@ -258,34 +258,41 @@ __device__ __forceinline__ void epilogue_chunk(const LinearArgs& p, LinearCtl& c
       if (m_base + j < p.M) p.acc_out[(size_t)(m_base + j) * p.N + n] = acc[j];
   }
   if (p.epilogue == NPL_EPI_SILU_MUL) {
-    // rows 0-63 gate, 64-127 up of output columns n_tile*64 + (row % 64)
+    // rows 0-63 gate, 64-127 up of output columns n_tile*64 + (row % 64).
+    // Gate row r and up row r + 64 split the chunk: the up row hands its
+    // values of tokens 0-3 to the gate row and the gate row its values of
+    // tokens 4-7 to the up row (one shared-memory exchange); each then
+    // finishes SiLU(g) * u for its 4 tokens, so all 128 threads work.
     const float sw = e.sw;
-    if (row >= 64) {
+    const bool gate = row < 64;
+    const int pr = row & 63;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
+    for (int j = 0; j < 8; ++j) {
+      if (gate == (j >= 4)) {
         const int m = min(m_base + j, p.M - 1);
-        c.xchg[j][row - 64] = __float2half_rn(dequant(acc[j], sa[m], sw, p.bias, e.bias));
+        c.xchg[j][gate ? 64 + pr : pr] = __float2half_rn(dequant(acc[j], sa[m], sw, p.bias, e.bias));
       }
     }
     epi_bar();
-    if (row < 64) {  // two full warps
-      const int col = n_tile * 64 + row;
-      __half* out = static_cast<__half*>(p.out);
+    const int col = n_tile * 64 + pr;
+    __half* out = static_cast<__half*>(p.out);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int m = m_base + j;
-        float h = 0.f;
-        if (m < p.M) {
-          const float g = __half2float(__float2half_rn(dequant(acc[j], sa[m], sw, p.bias, e.bias)));
-          const float u = __half2float(c.xchg[j][row]);
-          const __half hh = __float2half_rn(__fmul_rn(silu_h(g), u));
-          out[(size_t)m * p.ld_out + col] = hh;
-          h = fabsf(__half2float(hh));
-        }
-        if (p.absmax_out) {
-          h = warp_max(h);
-          if (lane == 0 && m < p.M) atomic_max_nonneg(p.absmax_out + m, h);
-        }
+    for (int jj = 0; jj < 4; ++jj) {
+      const int j = gate ? jj : jj + 4;
+      const int m = m_base + j;
+      float h = 0.f;
+      if (m < p.M) {
+        const float own = __half2float(__float2half_rn(dequant(acc[j], sa[m], sw, p.bias, e.bias)));
+        const float other = __half2float(c.xchg[j][gate ? pr : 64 + pr]);
+        const float g = gate ? own : other;
+        const float u = gate ? other : own;
+        const __half hh = __float2half_rn(__fmul_rn(silu_h(g), u));
+        out[(size_t)m * p.ld_out + col] = hh;
+        h = fabsf(__half2float(hh));
+      }
+      if (p.absmax_out) {
+        h = warp_max(h);
+        if (lane == 0 && m < p.M) atomic_max_nonneg(p.absmax_out + m, h);
       }
     }
     epi_bar();
