@@ -358,6 +358,66 @@ __device__ __forceinline__ void epilogue_chunk(const LinearArgs& p, LinearCtl& c
   }
 }
 
+// SiLU * up epilogue of 16 token columns [c0, c0 + 16): two 8-token chunks
+// through ONE shared-memory exchange (two barriers per 16 tokens). In the
+// single-chunk epilogue each exchange row uses half its columns: [j][r] for
+// tokens j < 4 (up -> gate) and [j][64 + r] for j >= 4 (gate -> up). The
+// second chunk takes the other halves. Same arithmetic as epilogue_chunk.
+template <int NT>
+__device__ __forceinline__ void silu_pair(const LinearArgs& p, LinearCtl& c, const float* sa, int m_tile, int n_tile,
+                                          int row, int c0, const int32_t (&a0)[8], const int32_t (&a1)[8],
+                                          const EpiOperands& e) {
+  const int n = n_tile * kTileN + row;
+  const int m_base = m_tile * NT + c0;
+  const int lane = threadIdx.x & 31;
+  if (p.acc_out && n < p.N) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (m_base + j < p.M) p.acc_out[(size_t)(m_base + j) * p.N + n] = a0[j];
+      if (m_base + 8 + j < p.M) p.acc_out[(size_t)(m_base + 8 + j) * p.N + n] = a1[j];
+    }
+  }
+  const float sw = e.sw;
+  const bool gate = row < 64;
+  const int pr = row & 63;
+  const int s_mine = gate ? 64 + pr : pr;  // chunk 0 hand-over slot; chunk 1 uses the other half
+  const int s_other = gate ? pr : 64 + pr;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    if (gate == (j >= 4)) {
+      const int m0 = min(m_base + j, p.M - 1), m1 = min(m_base + 8 + j, p.M - 1);
+      c.xchg[j][s_mine] = __float2half_rn(dequant(a0[j], sa[m0], sw, p.bias, e.bias));
+      c.xchg[j][s_other] = __float2half_rn(dequant(a1[j], sa[m1], sw, p.bias, e.bias));
+    }
+  }
+  epi_bar();
+  const int col = n_tile * 64 + pr;
+  __half* out = static_cast<__half*>(p.out);
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+#pragma unroll
+    for (int jj = 0; jj < 4; ++jj) {
+      const int j = gate ? jj : jj + 4;
+      const int m = m_base + 8 * h + j;
+      float a = 0.f;
+      if (m < p.M) {
+        const float own = __half2float(__float2half_rn(dequant(h ? a1[j] : a0[j], sa[m], sw, p.bias, e.bias)));
+        const float other = __half2float(c.xchg[j][h ? s_mine : s_other]);
+        const float g = gate ? own : other;
+        const float u = gate ? other : own;
+        const __half hh = __float2half_rn(__fmul_rn(silu_h(g), u));
+        out[(size_t)m * p.ld_out + col] = hh;
+        a = fabsf(__half2float(hh));
+      }
+      if (p.absmax_out) {
+        a = warp_max(a);
+        if (lane == 0 && m < p.M) atomic_max_nonneg(p.absmax_out + m, a);
+      }
+    }
+  }
+  epi_bar();
+}
+
 // Residual epilogue of 8 token columns [c0, c0 + 8) of tile row `row`, with
 // the chunk's residuals already in registers: out = fp16(fp16(v) + res).
 template <int NT>
@@ -390,6 +450,15 @@ __device__ __forceinline__ void residual_chunk(const LinearArgs& p, const float*
 template <int NT, typename AccFn>
 __device__ __forceinline__ void epilogue_tile(const LinearArgs& p, LinearCtl& c, const float* sa, int m_tile,
                                               int n_tile, int row, const EpiOperands& e, AccFn&& get_acc) {
+  if (NT >= 16 && p.epilogue == NPL_EPI_SILU_MUL) {
+    for (int c0 = 0; c0 < NT; c0 += 16) {
+      int32_t a0[8], a1[8];
+      get_acc(c0, a0);
+      get_acc(c0 + 8, a1);
+      silu_pair<NT>(p, c, sa, m_tile, n_tile, row, c0, a0, a1, e);
+    }
+    return;
+  }
   if (p.epilogue != NPL_EPI_RESIDUAL) {
     for (int c0 = 0; c0 < NT; c0 += 8) {
       int32_t acc[8];
