@@ -87,6 +87,33 @@ int npl_quant_rows_absmax(const void* x, int x_dtype, int rows, int cols, int ld
                           int8_t* q, int ldq, float* scale, void* stream);
 
 /*
+ * quantize_symmetric with a caller-given fp32 scale (w8a8.py:33-43, the
+ * static per-tensor mode of :94-103 and any precomputed per-token scale):
+ *   q[r, c] = clamp(rint(x[r, c] / scale[r * scale_stride]), -127, 127)
+ * with the IEEE fp32 quotient; scale_stride 1 = one scale per row, 0 = one
+ * scale for the whole tensor. The caller checks scale > 0 (the reference
+ * raises ValueError). Same shape and alignment rules as npl_quant_rows.
+ */
+int npl_quant_given_scale(const void* x, int x_dtype, int rows, int cols, int ldx, const float* scale,
+                          int scale_stride, int8_t* q, int ldq, void* stream);
+
+/*
+ * QDQ values of int8 rows: out[r, c] = fp32(q[r, c]) * scale[r * scale_stride]
+ * stored as out_dtype (NPL_F32, or NPL_F16 rounded once): the dequantised
+ * weight of w8a8.py:53-62 per_output_weight_qdq and the activation QDQ of
+ * :101-103 static_activation_qdq / :106-115 dynamic_per_token_activation_qdq.
+ * cols, ldq, ld_out multiples of 16; pointers 16-byte aligned.
+ */
+int npl_dequant_rows(const int8_t* q, int rows, int cols, int ldq, const float* scale, int scale_stride, void* out,
+                     int ld_out, int out_dtype, void* stream);
+
+/*
+ * scale_from_absmax (w8a8.py:46-50) over n fp32 absmax values:
+ *   scale[i] = max(fp32(fp16(max(absmax[i], fp16.tiny) / 127)), fp16.tiny)
+ */
+int npl_scale_from_absmax(const float* absmax, int n, float* scale, void* stream);
+
+/*
  * Dequantisation of int32 accumulators, as the epilogue of npl_w8a8_linear
  * (w8a8.py:118-139): v = ((acc[m, n] * sa[m]) * sw[n]) (+ bias[n]);
  * NPL_EPI_NONE writes v as out_dtype, NPL_EPI_RESIDUAL writes

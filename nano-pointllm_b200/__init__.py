@@ -5,9 +5,12 @@ name ``nanopointllm_b200`` (the entry points register it with importlib).
 
 Public surface, mirroring the reference ``nanopointllm`` API for this path:
 
-* ``nanopointllm_b200.w8a8``            - the W8A8 contract on the GPU
-  (quantize_symmetric, scale_from_absmax, per_output_weight_quant,
-  dynamic_per_token_quant, integer_linear_per_output, W8A8Linear)
+* ``nanopointllm_b200.w8a8``            - the W8A8 contract on the GPU under
+  the reference's names and signatures (quantize_symmetric,
+  scale_from_absmax, per_output_weight_qdq, static_activation_scale,
+  static_activation_qdq, dynamic_per_token_activation_qdq,
+  integer_linear_per_output_reference), plus the decode-path forms
+  (per_output_weight_quant, dynamic_per_token_quant, linear_q, W8A8Linear)
 * ``nanopointllm_b200.paged_attention`` - store_kvcache, paged_decode_attention,
   rope_store_kvcache
 * ``nanopointllm_b200.runner``          - W8A8 Llama decode runner

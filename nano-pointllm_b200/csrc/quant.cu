@@ -188,6 +188,78 @@ __global__ void __launch_bounds__(kNormThreads)
   }
 }
 
+// quantize_symmetric with a caller-given scale (w8a8.py:33-43): one fp32
+// scale per row (scale_stride 1) or one for the whole tensor (stride 0),
+// q = clamp(rint(v / s), -127, 127) with the IEEE quotient of every element
+// (the given scale need not be an fp16 value, so no reciprocal shortcut).
+// Grid (rows, ceil(cols / 2048)), 256 threads x 8 elements.
+template <typename T>
+__global__ void __launch_bounds__(256) quant_given_scale_kernel(const T* __restrict__ x, int cols, int ldx,
+                                                                const float* __restrict__ scale, int scale_stride,
+                                                                int8_t* __restrict__ q, int ldq) {
+  pdl_wait();
+  pdl_trigger();
+  const int r = blockIdx.x;
+  const float s = scale[(size_t)r * scale_stride];
+  const T* row = x + (size_t)r * ldx;
+  int8_t* qrow = q + (size_t)r * ldq;
+  const int c0 = (blockIdx.y * 256 + threadIdx.x) * 8;
+  if (c0 >= cols) return;
+  float v[8];
+  if constexpr (Vec<T>::N == 8) {
+    Vec<T>::load(row + c0, v);
+  } else {
+    float a[4], b[4];
+    Vec<T>::load(row + c0, a);
+    Vec<T>::load(row + c0 + 4, b);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) { v[i] = a[i]; v[4 + i] = b[i]; }
+  }
+  int qi[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) qi[i] = max(-127, min(127, __float2int_rn(__fdiv_rn(v[i], s))));
+  store_q<8>(qrow + c0, qi);
+}
+
+// Dequantisation of int8 rows: out = fp32(q) * s (one fp32 rounding), stored
+// as out_dtype; the QDQ value of w8a8.py:53-62 (per_output_weight_qdq) and
+// :101-103,106-115 (static / dynamic activation QDQ). Same grid as above.
+__global__ void __launch_bounds__(256) dequant_rows_kernel(const int8_t* __restrict__ q, int cols, int ldq,
+                                                           const float* __restrict__ scale, int scale_stride,
+                                                           void* __restrict__ out, int ld_out, int out_dtype) {
+  pdl_wait();
+  pdl_trigger();
+  const int r = blockIdx.x;
+  const float s = scale[(size_t)r * scale_stride];
+  const int c0 = (blockIdx.y * 256 + threadIdx.x) * 8;
+  if (c0 >= cols) return;
+  const uint2 packed = *reinterpret_cast<const uint2*>(q + (size_t)r * ldq + c0);
+  const int8_t* b = reinterpret_cast<const int8_t*>(&packed);
+  float v[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __fmul_rn((float)b[i], s);
+  if (out_dtype == NPL_F32) {
+    float4* o = reinterpret_cast<float4*>(static_cast<float*>(out) + (size_t)r * ld_out + c0);
+    o[0] = make_float4(v[0], v[1], v[2], v[3]);
+    o[1] = make_float4(v[4], v[5], v[6], v[7]);
+  } else {
+    uint4 h;
+    __half2* hp = reinterpret_cast<__half2*>(&h);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) hp[i] = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+    *reinterpret_cast<uint4*>(static_cast<__half*>(out) + (size_t)r * ld_out + c0) = h;
+  }
+}
+
+// scale_from_absmax (w8a8.py:46-50) elementwise over n fp32 values.
+__global__ void __launch_bounds__(256) scale_from_absmax_kernel(const float* __restrict__ absmax, int n,
+                                                                float* __restrict__ scale) {
+  pdl_wait();
+  pdl_trigger();
+  const int i = blockIdx.x * 256 + threadIdx.x;
+  if (i < n) scale[i] = scale_from_absmax(absmax[i]);
+}
+
 // out[m, n] = ((acc * sa[m]) * sw[n]) + bias[n], as the linear's epilogue
 // (NPL_EPI_NONE to out_dtype; NPL_EPI_RESIDUAL: fp16(fp16(v) + residual)).
 // Grid (M, ceil(N / 256)), one element per thread.
@@ -261,6 +333,49 @@ extern "C" int npl_quant_rows_absmax(const void* x, int x_dtype, int rows, int c
   if (!absmax_in || !q) return fail(NPL_ERR_ARG, "npl_quant_rows_absmax: null pointer");
   return quant_rows_common("npl_quant_rows_absmax", x, x_dtype, rows, cols, ldx, absmax_in, nullptr, q, ldq, scale,
                            stream);
+}
+
+extern "C" int npl_quant_given_scale(const void* x, int x_dtype, int rows, int cols, int ldx, const float* scale,
+                                     int scale_stride, int8_t* q, int ldq, void* stream) {
+  if (int rc = check_device()) return rc;
+  if (!x || !scale || !q) return fail(NPL_ERR_ARG, "npl_quant_given_scale: null pointer");
+  if (rows < 0 || cols <= 0 || cols % 16 || ldx < cols || ldx % 16 || ldq < cols || ldq % 16 ||
+      (scale_stride != 0 && scale_stride != 1))
+    return fail(NPL_ERR_ARG, "npl_quant_given_scale: bad shape rows=%d cols=%d ldx=%d ldq=%d scale_stride=%d", rows,
+                cols, ldx, ldq, scale_stride);
+  if (!aligned16(x) || !aligned16(q)) return fail(NPL_ERR_ARG, "npl_quant_given_scale: pointers must be 16-byte aligned");
+  if (rows == 0) return NPL_OK;
+  const dim3 grid(rows, (cols + 2047) / 2048);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (x_dtype == NPL_F32)
+    return launch_pdl("npl_quant_given_scale", quant_given_scale_kernel<float>, grid, dim3(256), 0, st,
+                      static_cast<const float*>(x), cols, ldx, scale, scale_stride, q, ldq);
+  if (x_dtype == NPL_F16)
+    return launch_pdl("npl_quant_given_scale", quant_given_scale_kernel<__half>, grid, dim3(256), 0, st,
+                      static_cast<const __half*>(x), cols, ldx, scale, scale_stride, q, ldq);
+  return fail(NPL_ERR_ARG, "npl_quant_given_scale: x_dtype must be NPL_F32 or NPL_F16");
+}
+
+extern "C" int npl_dequant_rows(const int8_t* q, int rows, int cols, int ldq, const float* scale, int scale_stride,
+                                void* out, int ld_out, int out_dtype, void* stream) {
+  if (int rc = check_device()) return rc;
+  if (!q || !scale || !out) return fail(NPL_ERR_ARG, "npl_dequant_rows: null pointer");
+  if (rows < 0 || cols <= 0 || cols % 16 || ldq < cols || ldq % 16 || ld_out < cols || ld_out % 16 ||
+      (scale_stride != 0 && scale_stride != 1) || (out_dtype != NPL_F32 && out_dtype != NPL_F16))
+    return fail(NPL_ERR_ARG, "npl_dequant_rows: bad shape rows=%d cols=%d ldq=%d ld_out=%d", rows, cols, ldq,
+                ld_out);
+  if (!aligned16(q) || !aligned16(out)) return fail(NPL_ERR_ARG, "npl_dequant_rows: pointers must be 16-byte aligned");
+  if (rows == 0) return NPL_OK;
+  return launch_pdl("npl_dequant_rows", dequant_rows_kernel, dim3(rows, (cols + 2047) / 2048), dim3(256), 0,
+                    static_cast<cudaStream_t>(stream), q, cols, ldq, scale, scale_stride, out, ld_out, out_dtype);
+}
+
+extern "C" int npl_scale_from_absmax(const float* absmax, int n, float* scale, void* stream) {
+  if (int rc = check_device()) return rc;
+  if (!absmax || !scale || n < 0) return fail(NPL_ERR_ARG, "npl_scale_from_absmax: bad arguments");
+  if (n == 0) return NPL_OK;
+  return launch_pdl("npl_scale_from_absmax", scale_from_absmax_kernel, dim3((n + 255) / 256), dim3(256), 0,
+                    static_cast<cudaStream_t>(stream), absmax, n, scale);
 }
 
 extern "C" int npl_dequant(const int32_t* acc, int ld_acc, const float* sa, const float* sw, const float* bias,

@@ -92,6 +92,19 @@ def rmsnorm_quant(x: torch.Tensor, weight: torch.Tensor, eps: float, residual: t
     return q, s, sum_out
 
 
+def shape_from_hf_config(cfg) -> LlamaShape:
+    """LlamaShape of an HF LlamaConfig (transformers 4.x rope_theta or 5.x
+    rope_parameters; head_dim defaults to hidden / heads)."""
+    head_dim = getattr(cfg, "head_dim", None) or cfg.hidden_size // cfg.num_attention_heads
+    rope = getattr(cfg, "rope_parameters", None) or {}
+    theta = rope.get("rope_theta", getattr(cfg, "rope_theta", 10000.0))
+    kv_heads = getattr(cfg, "num_key_value_heads", None) or cfg.num_attention_heads
+    return LlamaShape(hidden=cfg.hidden_size, heads=cfg.num_attention_heads, kv_heads=kv_heads,
+                      head_dim=head_dim, intermediate=cfg.intermediate_size, layers=cfg.num_hidden_layers,
+                      vocab=cfg.vocab_size, rope_theta=float(theta), eps=cfg.rms_norm_eps,
+                      max_position=cfg.max_position_embeddings)
+
+
 class W8A8Layer:
     def __init__(self, shape: LlamaShape, src, idx: int, device: torch.device,
                  k_cache: torch.Tensor, v_cache: torch.Tensor):
@@ -126,9 +139,16 @@ class W8A8LlamaRunner:
 
     def __init__(self, shape: LlamaShape, state_dict: dict[str, torch.Tensor], *, device: torch.device,
                  kv_pool: torch.Tensor | None = None, num_blocks: int = 0, block_size: int = 256,
-                 fuse_mlp_quant: bool = False):
+                 fuse_mlp_quant: bool = False, forward_context=None):
+        """``forward_context``: a callable returning the current step's
+        context. Default: this module's get_forward_context. The reference
+        engine passes its own nanopointllm.engine.forward_context.
+        get_forward_context; its ForwardContext (forward_context.py:10-24) is
+        read as it is, through the fields slot_mapping, block_tables,
+        context_lens, position_ids and seq_lens."""
         self.shape = shape
         self.device = torch.device(device)
+        self.forward_context = forward_context or get_forward_context
         # fuse_mlp_quant, decode batches (<= 64 tokens): the gate/up epilogue
         # also records each token's absmax of SiLU(gate)*up, and down quantises
         # its fp16 input itself, so no separate quantisation kernel runs between
@@ -167,19 +187,16 @@ class W8A8LlamaRunner:
             src.close()
 
     @classmethod
-    def from_hf(cls, hf_model, kv_pool: torch.Tensor, device: torch.device | None = None) -> "W8A8LlamaRunner":
+    def from_hf(cls, hf_model, kv_pool: torch.Tensor, device: torch.device | None = None,
+                forward_context=None) -> "W8A8LlamaRunner":
         """Build from an HF LlamaForCausalLM (the engine's model) and the
-        engine's KV pool tensor (KVPool.pool, kv_pool.py:9-24)."""
-        cfg = hf_model.config
-        head_dim = getattr(cfg, "head_dim", None) or cfg.hidden_size // cfg.num_attention_heads
-        rope = getattr(cfg, "rope_parameters", None) or {}
-        shape = LlamaShape(hidden=cfg.hidden_size, heads=cfg.num_attention_heads,
-                           kv_heads=cfg.num_key_value_heads, head_dim=head_dim,
-                           intermediate=cfg.intermediate_size, layers=cfg.num_hidden_layers,
-                           vocab=cfg.vocab_size, rope_theta=float(rope.get("rope_theta", 10000.0)),
-                           eps=cfg.rms_norm_eps, max_position=cfg.max_position_embeddings)
+        engine's KV pool tensor (KVPool.pool, kv_pool.py:9-24); every Linear
+        of the model is quantised per output channel once, here.
+        ``forward_context`` as the constructor's."""
+        shape = shape_from_hf_config(hf_model.config)
         device = device or kv_pool.device
-        return cls(shape, dict(hf_model.state_dict()), device=device, kv_pool=kv_pool)
+        return cls(shape, dict(hf_model.state_dict()), device=device, kv_pool=kv_pool,
+                   forward_context=forward_context)
 
     # ------------------------------------------------------------- layers
     def _attention_q(self, layer: W8A8Layer, q: torch.Tensor, ctx: ForwardContext):
@@ -268,7 +285,7 @@ class W8A8LlamaRunner:
     @torch.inference_mode()
     def forward(self, input_ids: torch.Tensor | None = None, *, inputs_embeds: torch.Tensor | None = None,
                 position_ids: torch.Tensor | None = None, last_only: bool = False) -> torch.Tensor:
-        ctx = get_forward_context()
+        ctx = self.forward_context()
         if ctx is None:
             raise RuntimeError("W8A8LlamaRunner.forward needs a ForwardContext (set_forward_context)")
         if inputs_embeds is None:

@@ -36,6 +36,7 @@ from . import package as P
 from . import paged_attention as PA
 from . import w8a8 as W
 from .rope import rope_tables
+from . import runner as R
 from .runner import ForwardContext, W8A8LlamaRunner, rmsnorm_quant
 from .synthetic import LlamaShape
 
@@ -205,17 +206,19 @@ class W8A8TPLlamaRunner(W8A8LlamaRunner):
 
     def __init__(self, shape: LlamaShape, state_dict: dict[str, torch.Tensor], *, device: torch.device,
                  group: dist.ProcessGroup | None = None, num_blocks: int = 0, block_size: int = 256,
-                 kv_pool: torch.Tensor | None = None, peer_exchange: bool = True):
+                 kv_pool: torch.Tensor | None = None, peer_exchange: bool = True, forward_context=None):
         """``peer_exchange``: decode batches (<= 64 tokens) exchange the
         row-parallel absmax and int32 partials through NVLink peer memory
         (PeerExchange) instead of NCCL all-reduces; larger batches use NCCL.
-        Results are identical either way."""
+        Results are identical either way. ``forward_context`` as
+        W8A8LlamaRunner's."""
         self.group = group if group is not None else dist.group.WORLD
         self.plan = tp_plan(shape, dist.get_rank(self.group), dist.get_world_size(self.group))
         self.full_shape = shape
         # the local geometry the attention path sees
         self.shape = replace(shape, heads=self.plan.hl, kv_heads=self.plan.kvl)
         self.device = torch.device(device)
+        self.forward_context = forward_context or R.get_forward_context
         self.fuse_mlp_quant = False
         self.timer = None
         if kv_pool is None:

@@ -118,9 +118,10 @@ def per_output_weight_quant(weight: torch.Tensor) -> tuple[torch.Tensor, torch.T
     """w8a8.py:53-62 (per_output_weight_qdq): (qweight int8 [N, K], scales fp32 [N])."""
     if weight.dim() < 2:
         raise ValueError("weight must have at least two dimensions")
-    w = weight.detach().reshape(weight.shape[0], -1)
-    q, s = dynamic_per_token_quant(w)
-    return q.reshape(weight.shape), s.reshape(-1)
+    w = _as_f16_or_f32(weight.detach()).reshape(weight.shape[0], -1)
+    k = w.shape[1]
+    q, s = dynamic_per_token_quant(_pad_cols(w))
+    return q[:, :k].reshape(weight.shape), s.reshape(-1)
 
 
 def linear_workspace(device: torch.device, m: int, n: int, k: int) -> torch.Tensor:
@@ -208,20 +209,181 @@ def linear_ex(qweight: torch.Tensor, wscale: torch.Tensor, *, x_mode: int, m: in
 
 
 def integer_linear_per_output(values: torch.Tensor, weight: torch.Tensor, *,
+                              activation_scale: torch.Tensor | float | None = None,
                               bias: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
-    """GPU counterpart of w8a8.py:118-139 with dynamic per-token activation
-    scales (the dynamic_per_token mode): returns (out fp32, acc int32)."""
+    """w8a8.py:118-139 on the GPU: returns (out fp32, acc int32).
+
+    ``activation_scale`` None quantises each token with its own dynamic scale
+    (the dynamic_per_token mode); a given scale (one value, or one per token)
+    is used as is, as integer_linear_per_output_reference does."""
+    if activation_scale is None:
+        _require_cuda(values, weight)
+        if values.shape[-1] != weight.shape[1] or weight.dim() != 2:
+            raise ValueError("linear input/weight shapes do not match")
+        k = values.shape[-1]
+        qa, sa = dynamic_per_token_quant(_pad_cols(_as_f16_or_f32(values).reshape(-1, k)))
+        qa, sa = qa[:, :k], sa.reshape(-1)
+    else:
+        return integer_linear_per_output_reference(values, weight, activation_scale=activation_scale, bias=bias)
+    return _integer_linear(qa, sa, weight, bias, values.shape[:-1])
+
+
+# --------------------------------------------------------------------------
+# The reference's contract functions under their own names and signatures
+# (w8a8.py:33-139), each running the library's kernels.
+# --------------------------------------------------------------------------
+
+def _as_f16_or_f32(values: torch.Tensor) -> torch.Tensor:
+    """The kernels read fp16 or fp32; any other float type is widened to fp32
+    first, exactly (the reference computes on values.float())."""
+    return values if values.dtype in _DT else values.float()
+
+
+def _pad_cols(t: torch.Tensor, multiple: int = 16) -> torch.Tensor:
+    """[rows, K] -> [rows, ceil(K / 16) * 16] with zero columns appended (a
+    zero column changes no absmax, quantises to 0 and adds 0 to every dot
+    product); the kernels need 16-element rows."""
+    k = t.shape[-1]
+    kp = -(-k // multiple) * multiple
+    if kp == k and t.stride(-1) == 1 and t.stride(0) % 16 == 0:
+        return t
+    out = torch.zeros((t.shape[0], kp), dtype=t.dtype, device=t.device)
+    out[:, :k] = t
+    return out
+
+
+def _scale_operand(scale: torch.Tensor | float, rows: int, device: torch.device) -> tuple[torch.Tensor, int]:
+    """A quantisation scale as the kernels take it: (fp32 [1] with stride 0)
+    for one tensor-wide value, (fp32 [rows] with stride 1) for one per row."""
+    s = torch.as_tensor(scale, dtype=torch.float32, device=device).detach().float()
+    if bool((s <= 0).any()):  # w8a8.py:38-39
+        raise ValueError("quantization scale must be positive")
+    if s.numel() == 1:
+        return s.reshape(1).contiguous(), 0
+    if s.numel() == rows:
+        return s.reshape(rows).contiguous(), 1
+    raise ValueError(f"scale must hold one value or one per row ({rows}), got shape {tuple(s.shape)}")
+
+
+def quantize_symmetric(values: torch.Tensor, scale: torch.Tensor | float) -> torch.Tensor:
+    """w8a8.py:33-43: int8(clamp(round(values.float() / scale.float()), -127,
+    127)), ties to even, one IEEE fp32 division per element. ``scale`` is one
+    value or one per row of the last dimension (shape [..., 1] or [...]);
+    ValueError if any scale is <= 0."""
+    _require_cuda(values)
+    if values.dim() == 0:
+        values = values.reshape(1, 1)
+    x = _as_f16_or_f32(values)
+    k = x.shape[-1]
+    rows = x.reshape(-1, k)
+    sp, stride = _scale_operand(scale, rows.shape[0], x.device)
+    xp = _pad_cols(rows)
+    q = torch.empty(xp.shape, dtype=torch.int8, device=x.device)
+    if rows.shape[0]:
+        L.check(L.lib.npl_quant_given_scale(xp.data_ptr(), _DT[xp.dtype], xp.shape[0], xp.shape[1], xp.stride(0),
+                                            sp.data_ptr(), stride, q.data_ptr(), q.stride(0), L.stream_ptr(x.device)))
+    return q[:, :k].reshape(values.shape)
+
+
+def scale_from_absmax(absmax: torch.Tensor) -> torch.Tensor:
+    """w8a8.py:46-50: fp32(fp16(max(absmax, fp16.tiny) / 127)), >= fp16.tiny,
+    elementwise (same shape as ``absmax``)."""
+    _require_cuda(absmax)
+    a = absmax.detach().float().contiguous()
+    out = torch.empty_like(a)
+    L.check(L.lib.npl_scale_from_absmax(a.data_ptr(), a.numel(), out.data_ptr(), L.stream_ptr(a.device)))
+    return out
+
+
+def _dequant_rows(q: torch.Tensor, scale: torch.Tensor, stride: int, dtype: torch.dtype) -> torch.Tensor:
+    """fp32(q) * scale per row (npl_dequant_rows), returned as ``dtype``
+    (fp16 rounded once in the kernel; other types through fp32)."""
+    k = q.shape[-1]
+    qp = _pad_cols(q.reshape(-1, k))
+    out_dt = torch.float16 if dtype == torch.float16 else torch.float32
+    out = torch.empty(qp.shape, dtype=out_dt, device=q.device)
+    if qp.shape[0]:
+        L.check(L.lib.npl_dequant_rows(qp.data_ptr(), qp.shape[0], qp.shape[1], qp.stride(0), scale.data_ptr(),
+                                       stride, out.data_ptr(), out.stride(0), _DT[out_dt], L.stream_ptr(q.device)))
+    return out[:, :k].reshape(q.shape).to(dtype)
+
+
+def per_output_weight_qdq(weight: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """w8a8.py:53-62: (dequantised weight in weight.dtype, int8 weight of the
+    same shape, fp32 per-output-channel scales [N])."""
+    _require_cuda(weight)
+    q, s = per_output_weight_quant(weight)
+    deq = _dequant_rows(q.reshape(weight.shape[0], -1), s, 1, weight.dtype)
+    return deq.reshape(weight.shape), q, s
+
+
+def static_activation_scale(absmax: float | torch.Tensor, device: torch.device | None = None) -> torch.Tensor:
+    """w8a8.py:94-99: the tensor-wide scale of one absmax, a 0-dim fp32 CUDA
+    tensor (on ``device``, or the absmax's device, or the current one)."""
+    if device is None:
+        device = absmax.device if isinstance(absmax, torch.Tensor) and absmax.is_cuda else \
+            torch.device("cuda", torch.cuda.current_device())
+    value = torch.as_tensor(absmax, dtype=torch.float32, device=device)
+    if value.numel() != 1:
+        raise ValueError("static activation scale expects one tensor-wide absmax")
+    return scale_from_absmax(value.reshape(()))
+
+
+def static_activation_qdq(values: torch.Tensor, scale: torch.Tensor | float) -> torch.Tensor:
+    """w8a8.py:101-103: quantise with the given scale and dequantise, in
+    values.dtype."""
+    q = quantize_symmetric(values, scale)
+    k = q.shape[-1] if q.dim() else 1
+    sp, stride = _scale_operand(scale, q.numel() // max(1, k), values.device)
+    return _dequant_rows(q.reshape(-1, k), sp, stride, values.dtype).reshape(values.shape)
+
+
+def dynamic_per_token_activation_qdq(values: torch.Tensor, *, axis: int = -1) -> tuple[torch.Tensor, torch.Tensor]:
+    """w8a8.py:106-115: (QDQ values in values.dtype, fp32 scales with the
+    reduced axis kept as size 1), one scale per slice along ``axis``."""
+    if values.dim() == 0:
+        raise ValueError("dynamic per-token quantization expects a tensor")
+    _require_cuda(values)
+    ax = axis % values.dim()
+    v = values.movedim(ax, -1)
+    k = v.shape[-1]
+    rows = _pad_cols(_as_f16_or_f32(v).reshape(-1, k))
+    q, s = dynamic_per_token_quant(rows)
+    s = s.reshape(-1)
+    deq = _dequant_rows(q[:, :k], s, 1, values.dtype).reshape(v.shape).movedim(-1, ax)
+    return deq, s.reshape(*v.shape[:-1], 1).movedim(-1, ax)
+
+
+def _integer_linear(qa: torch.Tensor, sa: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None,
+                    lead: torch.Size) -> tuple[torch.Tensor, torch.Tensor]:
+    """int8 activations [rows, K] + fp32 per-row scales x the per-output
+    quantised ``weight`` -> (out fp32, acc int32) shaped [*lead, N]."""
+    qw, sw = per_output_weight_quant(weight)
+    k = qw.shape[1]
+    qa2 = _pad_cols(qa.reshape(-1, k))
+    qw = _pad_cols(qw)
+    acc = torch.empty((qa2.shape[0], qw.shape[0]), dtype=torch.int32, device=qw.device)
+    b = None if bias is None else bias.detach().float().contiguous()
+    out = linear_q(qa2, sa.contiguous(), qw, sw, bias=b, out_dtype=torch.float32, acc_out=acc)
+    return out.reshape(*lead, qw.shape[0]), acc.reshape(*lead, qw.shape[0])
+
+
+def integer_linear_per_output_reference(values: torch.Tensor, weight: torch.Tensor, *,
+                                        activation_scale: torch.Tensor | float,
+                                        bias: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """w8a8.py:118-139 with its signature, on the GPU: int8 activations from
+    ``activation_scale`` (one tensor-wide value -- the static mode -- or one
+    per token), per-output-channel int8 weights, int8 x int8 -> int32 on the
+    tensor cores, then ((acc * s_a) * s_w) + bias in fp32. Returns (out fp32,
+    acc int32), both [..., N]."""
     _require_cuda(values, weight)
     if values.shape[-1] != weight.shape[1] or weight.dim() != 2:
         raise ValueError("linear input/weight shapes do not match")
-    qa, sa = dynamic_per_token_quant(values)
-    qw, sw = per_output_weight_quant(weight)
-    qa2 = qa.reshape(-1, qa.shape[-1])
-    acc = torch.empty((qa2.shape[0], weight.shape[0]), dtype=torch.int32, device=values.device)
-    b = None if bias is None else bias.detach().float().contiguous()
-    out = linear_q(qa2, sa.reshape(-1), qw, sw, bias=b, out_dtype=torch.float32, acc_out=acc)
-    lead = values.shape[:-1]
-    return out.reshape(*lead, weight.shape[0]), acc.reshape(*lead, weight.shape[0])
+    qa = quantize_symmetric(values, activation_scale)
+    rows = qa.numel() // max(1, qa.shape[-1]) if qa.dim() else 1
+    sp, stride = _scale_operand(activation_scale, rows, values.device)
+    sa = sp.expand(rows) if stride == 0 else sp
+    return _integer_linear(qa, sa, weight, bias, values.shape[:-1])
 
 
 def pack_gate_up(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
@@ -244,17 +406,28 @@ class W8A8Linear:
     per_output_weight_qdq, activations from dynamic per-token quantisation).
     """
 
-    def __init__(self, qweight: torch.Tensor, wscale: torch.Tensor, bias: torch.Tensor | None = None):
+    def __init__(self, qweight: torch.Tensor, wscale: torch.Tensor, bias: torch.Tensor | None = None, *,
+                 activation_scale: torch.Tensor | float | None = None):
+        """``activation_scale``: None quantises each call's tokens with their
+        own dynamic scales (dynamic_per_token, w8a8.py:106-115); a given
+        tensor-wide value is the static mode (w8a8.py:94-103)."""
         if qweight.dtype != torch.int8 or qweight.dim() != 2:
             raise ValueError("qweight must be int8 [N, K]")
         self.qweight = qweight.contiguous()
         self.wscale = wscale.float().contiguous()
         self.bias = None if bias is None else bias.float().contiguous()
+        self.activation_scale = None
+        if activation_scale is not None:
+            s = torch.as_tensor(activation_scale, dtype=torch.float32, device=self.qweight.device)
+            if s.numel() != 1 or float(s) <= 0:
+                raise ValueError("a static activation scale is one positive value")
+            self.activation_scale = s.reshape(1).contiguous()
 
     @classmethod
-    def from_float(cls, weight: torch.Tensor, bias: torch.Tensor | None = None) -> "W8A8Linear":
+    def from_float(cls, weight: torch.Tensor, bias: torch.Tensor | None = None, *,
+                   activation_scale: torch.Tensor | float | None = None) -> "W8A8Linear":
         q, s = per_output_weight_quant(weight)
-        return cls(q, s, bias)
+        return cls(q, s, bias, activation_scale=activation_scale)
 
     @property
     def out_features(self) -> int:
@@ -265,7 +438,11 @@ class W8A8Linear:
         return self.qweight.shape[1]
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
-        qa, sa = dynamic_per_token_quant(x)
+        if self.activation_scale is None:
+            qa, sa = dynamic_per_token_quant(x)
+        else:
+            qa = quantize_symmetric(x, self.activation_scale)
+            sa = self.activation_scale.expand(qa.numel() // x.shape[-1]).contiguous()
         out = linear_q(qa.reshape(-1, x.shape[-1]), sa.reshape(-1), self.qweight, self.wscale, bias=self.bias,
                        out_dtype=torch.float16 if x.dtype == torch.float16 else torch.float32)
         return out.reshape(*x.shape[:-1], self.out_features)

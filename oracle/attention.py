@@ -40,6 +40,7 @@ def paged_varlen_attention(q, k_cache, v_cache, block_tables, context_lens, q_le
     bs = k_cache.shape[1]
     out = np.zeros((total_q, H, D), F16)
     scale = F32(scale)
+    head_kv = np.arange(H) // num_kv_groups
     for b in range(len(q_lens)):
         q_len, ctx, off = int(q_lens[b]), int(context_lens[b]), int(q_offsets[b])
         if q_len <= 0:
@@ -52,25 +53,28 @@ def paged_varlen_attention(q, k_cache, v_cache, block_tables, context_lens, q_le
         k_all = np.where(valid[:, None, None], k_cache[blk, keys % bs], 0).astype(F16)  # [n_pad, Hkv, D]
         v_all = np.where(valid[:, None, None], v_cache[blk, keys % bs], 0).astype(F16)
         q_pos = prefix + np.arange(q_len)
-        for h in range(H):
-            kvh = h // num_kv_groups
-            qh = q[off:off + q_len, h].astype(F64)
-            m = np.full(q_len, NEG, F32)
-            l = np.zeros(q_len, F32)
-            acc = np.zeros((q_len, D), F32)
-            for start in range(0, n_pad, block_n):
-                kt = k_all[start:start + block_n, kvh].astype(F64)
-                vt = v_all[start:start + block_n, kvh].astype(F64)
-                pos = start + np.arange(block_n)
-                s = (qh @ kt.T).astype(F32) * scale
-                allowed = (pos[None, :] < ctx) & (pos[None, :] <= q_pos[:, None])
-                s = np.where(allowed, s, NEG)
-                m_new = np.maximum(m, s.max(axis=1))
-                p = np.exp(s - m_new[:, None], dtype=F32)
-                alpha = np.exp(m - m_new, dtype=F32)
-                pv = (p.astype(F16).astype(F64) @ vt).astype(F32)
-                acc = acc * alpha[:, None] + pv
-                l = l * alpha + p.sum(axis=1, dtype=F32)
-                m = m_new
-            out[off:off + q_len, h] = (acc / l[:, None]).astype(F16)
+        # every head at once: [H, q_len, D] queries, [H, n_pad, D] keys/values
+        qh = q[off:off + q_len].astype(F64).transpose(1, 0, 2)
+        kh_all = k_all[:, head_kv].astype(F64).transpose(1, 0, 2)
+        vh_all = v_all[:, head_kv].astype(F64).transpose(1, 0, 2)
+        m = np.full((H, q_len), NEG, F32)
+        l = np.zeros((H, q_len), F32)
+        acc = np.zeros((H, q_len, D), F32)
+        for start in range(0, n_pad, block_n):
+            if start > q_pos[-1]:
+                break  # every key of this and later tiles is masked for every query: p = 0, alpha = 1
+            kt = kh_all[:, start:start + block_n]
+            vt = vh_all[:, start:start + block_n]
+            pos = start + np.arange(block_n)
+            s = (qh @ kt.transpose(0, 2, 1)).astype(F32) * scale
+            allowed = (pos[None, :] < ctx) & (pos[None, :] <= q_pos[:, None])
+            s = np.where(allowed[None], s, NEG)
+            m_new = np.maximum(m, s.max(axis=-1))
+            p = np.exp(s - m_new[..., None], dtype=F32)
+            alpha = np.exp(m - m_new, dtype=F32)
+            pv = (p.astype(F16).astype(F64) @ vt).astype(F32)
+            acc = acc * alpha[..., None] + pv
+            l = l * alpha + p.sum(axis=-1, dtype=F32)
+            m = m_new
+        out[off:off + q_len] = (acc / l[..., None]).astype(F16).transpose(1, 0, 2)
     return out

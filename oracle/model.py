@@ -25,18 +25,30 @@ F32 = np.float32
 
 
 class W8A8LlamaOracle:
-    def __init__(self, weights: dict, shape, k_cache_blocks: int, block_size: int, prefill: str = "exact"):
+    def __init__(self, weights: dict, shape, k_cache_blocks: int, block_size: int, prefill: str = "exact",
+                 varlen_block_n: int = 64, quantized: dict | None = None,
+                 decode_dtype=np.float64):
         """prefill: "exact" evaluates multi-token rows in float64 (the
         reference's CPU path, SDPA per sequence); "varlen" restates its CUDA
-        path, the Triton varlen kernel (oracle.attention)."""
+        path, the Triton varlen kernel (oracle.attention), with key tiles of
+        ``varlen_block_n`` (the kernel's BLOCK_N: 64 by default for head_dim
+        128, NANOPOINTLLM_VARLEN_BLOCK_N selects another, paged_attention.py:53-63).
+
+        ``quantized``: name -> (int8 [N, K], fp32 scales [N]) of Linears
+        already quantised per output channel (checked elsewhere against
+        per_output_weight_quant); ``weights`` then needs only the embedding
+        and the norms. ``decode_dtype``: arithmetic of single-token rows'
+        attention (float64, or the reference kernels' float32)."""
         if prefill not in ("exact", "varlen"):
             raise ValueError("prefill must be 'exact' or 'varlen'")
         self.prefill = prefill
+        self.varlen_block_n = varlen_block_n
+        self.decode_dtype = decode_dtype
         self.s = shape
         self.w = {k: np.asarray(v) for k, v in weights.items()}
-        self.q = {}
+        self.q = dict(quantized or {})
         for name, arr in self.w.items():
-            if arr.ndim == 2 and name != "model.embed_tokens.weight":
+            if arr.ndim == 2 and name != "model.embed_tokens.weight" and name not in self.q:
                 self.q[name] = O.per_output_weight_quant(arr)
         self.block_size = block_size
         kv_shape = (shape.layers, k_cache_blocks, block_size, shape.kv_heads, shape.head_dim)
@@ -66,7 +78,7 @@ class W8A8LlamaOracle:
             if pre:
                 va = OA.paged_varlen_attention(
                     q, kc, vc, np.asarray(block_tables)[pre], np.asarray(context_lens, np.int32)[pre],
-                    np.asarray(seq_lens, np.int32)[pre], starts[pre], scale, groups)
+                    np.asarray(seq_lens, np.int32)[pre], starts[pre], scale, groups, block_n=self.varlen_block_n)
                 for b in pre:
                     out[starts[b]:starts[b] + seq_lens[b]] = va[starts[b]:starts[b] + seq_lens[b]]
         for b, qlen in enumerate(seq_lens):
@@ -76,23 +88,29 @@ class W8A8LlamaOracle:
             n = int(context_lens[b])
             nblk = (n + self.block_size - 1) // self.block_size
             bt = block_tables[b, :nblk]
-            k = kc[bt].reshape(-1, s.kv_heads, s.head_dim)[:n].astype(np.float64)
-            v = vc[bt].reshape(-1, s.kv_heads, s.head_dim)[:n].astype(np.float64)
+            dt = self.decode_dtype if qlen == 1 else np.float64
+            k = kc[bt].reshape(-1, s.kv_heads, s.head_dim)[:n].astype(dt)
+            v = vc[bt].reshape(-1, s.kv_heads, s.head_dim)[:n].astype(dt)
             prefix = n - qlen
             for j in range(qlen):
                 visible = prefix + j + 1
                 for h in range(s.heads):
                     kh = h // groups
-                    sc = k[:visible, kh] @ q[off + j, h].astype(np.float64) * scale
+                    sc = k[:visible, kh] @ q[off + j, h].astype(dt) * dt(scale)
                     p = np.exp(sc - sc.max())
                     out[off + j, h] = (p[:, None] * v[:visible, kh]).sum(0) / p.sum()
             off += qlen
         return out.astype(F16)
 
-    def forward(self, ids, positions, slot_mapping, seq_lens, context_lens, block_tables):
-        """Returns fp16 logits [T, vocab] for the flattened new tokens."""
+    def forward(self, ids, positions, slot_mapping, seq_lens, context_lens, block_tables, *, embeds=None,
+                rows=None):
+        """Returns fp16 logits [T, vocab] for the flattened new tokens (only
+        for the token indices ``rows`` when given, as the runner's
+        ``last_only``). ``embeds`` [T, hidden] fp16 replaces the embedding
+        lookup of ``ids`` (the engine's inputs_embeds with point rows,
+        lightweight_runner.py:625-650)."""
         s = self.s
-        h = self.w["model.embed_tokens.weight"][np.asarray(ids)]
+        h = np.asarray(embeds, F16) if embeds is not None else self.w["model.embed_tokens.weight"][np.asarray(ids)]
         cos, sin = self.cos[positions], self.sin[positions]
         T = h.shape[0]
         for layer in range(s.layers):
@@ -112,12 +130,15 @@ class W8A8LlamaOracle:
             u = self.linear(p + "mlp.up_proj.weight", x)
             d = self.linear(p + "mlp.down_proj.weight", O.silu_mul(g, u))
             h = (h.astype(F32) + d.astype(F32)).astype(F16)
+        if rows is not None:
+            h = h[np.asarray(rows)]
         x = O.rmsnorm(h, self.w["model.norm.weight"], s.eps)
         return self.linear("lm_head.weight", x)
 
 
-def greedy_generate(oracle: W8A8LlamaOracle, prompts, block_tables, steps: int):
-    """Prefill all prompts in one flattened pass, then ``steps - 1`` batched
+def greedy_generate(oracle: W8A8LlamaOracle, prompts, block_tables, steps: int, embeds=None):
+    """Prefill all prompts in one flattened pass (``embeds`` [T, hidden]
+    replacing their embedding rows when given), then ``steps - 1`` batched
     decode steps; returns (tokens [steps, B], logits [steps, B, V] fp32)."""
     bs = oracle.block_size
     bt = np.asarray(block_tables)
@@ -130,10 +151,9 @@ def greedy_generate(oracle: W8A8LlamaOracle, prompts, block_tables, steps: int):
     ids = [t for p in prompts for t in p]
     pos = np.concatenate([np.arange(n) for n in lengths])
     slots = np.array([slot(b, p) for b, n in enumerate(lengths) for p in range(n)])
-    logits = oracle.forward(ids, pos, slots, lengths, lengths, bt)
     last = np.cumsum(lengths) - 1
+    lg = oracle.forward(ids, pos, slots, lengths, lengths, bt, embeds=embeds, rows=last).astype(F32)
     out_tok, out_logits = [], []
-    lg = logits[last].astype(F32)
     for _ in range(steps):
         nxt = lg.argmax(-1)
         out_tok.append(nxt.tolist())

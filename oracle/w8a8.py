@@ -70,14 +70,23 @@ def dynamic_per_token_quant(values) -> tuple[np.ndarray, np.ndarray]:
 def int_matmul_nt(qa: np.ndarray, qw: np.ndarray) -> np.ndarray:
     """w8a8.py:130-132: int32(qa) @ int32(qw).T.
 
-    Computed through float64 BLAS, which is exact here: every partial sum is an
-    integer of magnitude <= K * 127**2 < 2**53.
+    Evaluated with torch's CPU float32 matmul (the reference computes on torch
+    CPU too) over slices of 1024 columns, which is exact: every product is an
+    integer of magnitude <= 127**2 and every partial sum of a slice one of
+    magnitude <= 1024 * 127**2 < 2**24, so no fp32 rounding occurs in any
+    summation order; the slices are then added in int64.
     """
+    import torch
+
     k = qa.shape[-1]
     if k * QMAX * QMAX >= 1 << 31:  # w8a8.py:152-153
         raise OverflowError("worst-case dot product exceeds signed INT32")
-    acc = qa.reshape(-1, k).astype(np.float64) @ qw.astype(np.float64).T
-    return acc.astype(np.int32)
+    a32 = torch.from_numpy(np.ascontiguousarray(qa.reshape(-1, k))).float()
+    w32 = torch.from_numpy(np.ascontiguousarray(qw)).float()
+    acc = torch.zeros((a32.shape[0], w32.shape[0]), dtype=torch.int64)
+    for k0 in range(0, k, 1024):
+        acc += (a32[:, k0:k0 + 1024] @ w32[:, k0:k0 + 1024].T).long()
+    return acc.int().numpy()
 
 
 def dequantize(acc, act_scale, w_scale, bias=None) -> np.ndarray:
@@ -220,26 +229,29 @@ def store_kvcache(key, value, k_cache, v_cache, slot_mapping) -> None:
         v_cache[slot // block_size, slot % block_size] = value[t]
 
 
-def paged_decode_attention(q, k_cache, v_cache, block_tables, context_lens, scale, num_kv_groups=1):
-    """paged_attention.py:846-869 (_paged_decode_attention_pytorch) in fp64.
+def paged_decode_attention(q, k_cache, v_cache, block_tables, context_lens, scale, num_kv_groups=1,
+                           dtype=np.float64):
+    """paged_attention.py:846-869 (_paged_decode_attention_pytorch), evaluated
+    in ``dtype``: float64 (the exact reference point), or float32, the
+    arithmetic type the reference's SDPA and Triton decode kernels use.
 
-    q [B, H, D]; caches [num_blocks, block_size, Hkv, D]; returns fp64 [B, H, D].
-    A row with context_len 0 (a padded bucket row) returns zeros.
+    q [B, H, D]; caches [num_blocks, block_size, Hkv, D]; returns [B, H, D]
+    in ``dtype``. A row with context_len 0 (a padded bucket row) returns zeros.
     """
     B, H, D = q.shape
     block_size = k_cache.shape[1]
-    out = np.zeros((B, H, D), dtype=np.float64)
+    out = np.zeros((B, H, D), dtype=dtype)
     for b in range(B):
         n = int(context_lens[b])
         if n <= 0:
             continue
         nblk = (n + block_size - 1) // block_size
         bt = np.asarray(block_tables[b, :nblk])
-        k = k_cache[bt].reshape(-1, k_cache.shape[2], D)[:n].astype(np.float64)
-        v = v_cache[bt].reshape(-1, v_cache.shape[2], D)[:n].astype(np.float64)
+        k = k_cache[bt].reshape(-1, k_cache.shape[2], D)[:n].astype(dtype)
+        v = v_cache[bt].reshape(-1, v_cache.shape[2], D)[:n].astype(dtype)
         for h in range(H):
             kh = h // num_kv_groups
-            s = k[:, kh, :] @ q[b, h].astype(np.float64) * scale
+            s = k[:, kh, :] @ q[b, h].astype(dtype) * dtype(scale)
             p = np.exp(s - s.max())
             out[b, h] = (p[:, None] * v[:, kh, :]).sum(0) / p.sum()
     return out

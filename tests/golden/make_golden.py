@@ -36,7 +36,12 @@ import torch
 
 HERE = pathlib.Path(__file__).resolve().parent
 REPO = HERE.parent.parent
-REF = pathlib.Path(os.environ.get("NPL_REFERENCE", "/root/reference"))
+def _reference_root() -> pathlib.Path:
+    """The reference checkout, from NPL_REFERENCE (required: there is no default)."""
+    root = os.environ.get("NPL_REFERENCE")
+    if not root:
+        raise SystemExit("set NPL_REFERENCE to the root of the Nano-pointllm checkout")
+    return pathlib.Path(root)
 
 
 def _import_repo():
@@ -57,14 +62,53 @@ def f16(t: torch.Tensor) -> np.ndarray:
     return t.detach().to(torch.float16).numpy()
 
 
+def _static_linear(R, S) -> None:
+    """Integer golden with STATIC activation scales (w8a8.py:94-103 feeding
+    :118-139): one tensor-wide scale from the tensor's absmax, and a given
+    per-token scale that is not an fp16 value (a caller's own calibration),
+    fp16 and fp32 inputs with 1% outlier channels, with bias; plus the QDQ
+    outputs of static_activation_qdq, dynamic_per_token_activation_qdq and
+    per_output_weight_qdq."""
+    arrays = {}
+    for tag, (m, k, n, dtype, seed) in {
+        "tensor_f16": (6, 640, 272, torch.float16, 31),
+        "tensor_f32": (4, 1024, 96, torch.float32, 32),
+    }.items():
+        x, w = S.config1_inputs(seed=seed, m=m, k=k, n=n)
+        x, w = x.to(dtype), w.to(dtype)
+        g = torch.Generator().manual_seed(seed + 100)
+        bias = torch.randn(n, generator=g) * 0.1
+        s_tensor = R.static_activation_scale(x.float().abs().max())
+        out, acc = R.integer_linear_per_output_reference(x, w, activation_scale=s_tensor, bias=bias)
+        # per-token scales 0.9x the dynamic ones, kept in fp32 (not fp16 values)
+        s_tok = R.scale_from_absmax(x.float().abs().amax(-1, keepdim=True)) * 0.9
+        out_t, acc_t = R.integer_linear_per_output_reference(x, w, activation_scale=s_tok, bias=bias)
+        w_deq, qw, ws = R.per_output_weight_qdq(w)
+        x_qdq, x_s = R.dynamic_per_token_activation_qdq(x)
+        arrays.update({
+            # x, w: rebuilt at test time by synthetic.config1_inputs(seed, m, k, n)
+            f"{tag}_shape": np.array([m, k, n, seed], np.int64), f"{tag}_bias": bias.numpy(),
+            f"{tag}_s_tensor": s_tensor.numpy(), f"{tag}_out": out.numpy(), f"{tag}_acc": acc.numpy(),
+            f"{tag}_qa": R.quantize_symmetric(x, s_tensor).numpy(),
+            f"{tag}_x_static_qdq": R.static_activation_qdq(x, s_tensor).numpy(),
+            f"{tag}_s_tok": s_tok.numpy(), f"{tag}_out_tok": out_t.numpy(), f"{tag}_acc_tok": acc_t.numpy(),
+            f"{tag}_w_deq": w_deq.numpy(), f"{tag}_qw": qw.numpy(), f"{tag}_ws": ws.numpy(),
+            f"{tag}_x_dyn_qdq": x_qdq.numpy(), f"{tag}_x_dyn_s": x_s.numpy(),
+        })
+    np.savez_compressed(HERE / "static_linear.npz", **arrays)
+
+
 def main() -> None:
-    sys.path.insert(0, str(REF))
+    sys.path.insert(0, str(_reference_root()))
     os.environ.setdefault("PYTHONDONTWRITEBYTECODE", "1")
     _import_repo()
     from nanopointllm.compression import w8a8 as R
     from nanopointllm_b200 import synthetic as S
 
     torch.set_num_threads(max(1, os.cpu_count() or 1))
+    _static_linear(R, S)
+    if "--static-only" in sys.argv[1:]:
+        return
 
     # 1. Rounding/clipping KAT: the reference's own vector (tests/test_w8a8_contract.py:15-21).
     kat_in = torch.tensor([-200.0, -127.5, -2.5, -1.5, 1.5, 2.5, 127.5, 200.0])

@@ -25,7 +25,7 @@ import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
 HERE = pathlib.Path(__file__).resolve().parent
-REF = pathlib.Path(os.environ.get("NPL_REFERENCE", "/root/reference"))
+REF = os.environ.get("NPL_REFERENCE")  # root of the Nano-pointllm checkout (required)
 
 # (name, H, Hkv, D, block_size, [(q_len, ctx_len), ...], seed)
 CASES = [

@@ -239,3 +239,32 @@ def test_tiny_model_varlen_prefill_vs_exact_until_tie():
     oracle = OM.W8A8LlamaOracle(weights, shape, int(g["num_blocks"]), int(g["block_size"]), prefill="varlen")
     tokens, logits = OM.greedy_generate(oracle, prompts, g["block_tables"], steps=g["tokens"].shape[0])
     assert_match_until_tie(tokens, logits, g["tokens"], g["logits"], tie_tol=2e-2, atol=5e-2)
+
+
+@pytest.mark.parametrize("tag", ["tensor_f16", "tensor_f32"])
+def test_static_scale_linear_golden(tag):
+    """Static activation scales (w8a8.py:94-103 feeding :118-139): one
+    tensor-wide scale, and given per-token fp32 scales that are not fp16
+    values; the reference's outputs, int32 accumulators and QDQ values."""
+    from nanopointllm_b200 import synthetic as S
+    g = golden("static_linear.npz")
+    m, k, n, seed = (int(v) for v in g[f"{tag}_shape"])
+    dtype = torch.float16 if tag.endswith("f16") else torch.float32
+    x, w = (t.to(dtype).numpy() for t in S.config1_inputs(seed=seed, m=m, k=k, n=n))
+    bias = g[f"{tag}_bias"]
+    s = g[f"{tag}_s_tensor"]
+    np.testing.assert_array_equal(O.scale_from_absmax(np.abs(x.astype(np.float32)).max()), s)
+    np.testing.assert_array_equal(O.quantize_symmetric(x, s), g[f"{tag}_qa"])
+    out, acc = O.integer_linear_per_output_reference(x, w, activation_scale=s, bias=bias)
+    np.testing.assert_array_equal(acc, g[f"{tag}_acc"])
+    np.testing.assert_array_equal(out, g[f"{tag}_out"])
+    out, acc = O.integer_linear_per_output_reference(x, w, activation_scale=g[f"{tag}_s_tok"], bias=bias)
+    np.testing.assert_array_equal(acc, g[f"{tag}_acc_tok"])
+    np.testing.assert_array_equal(out, g[f"{tag}_out_tok"])
+    qw, ws = O.per_output_weight_quant(w)
+    np.testing.assert_array_equal(qw, g[f"{tag}_qw"])
+    np.testing.assert_array_equal(ws, g[f"{tag}_ws"])
+    np.testing.assert_array_equal((qw.astype(np.float32) * ws[:, None]).astype(w.dtype), g[f"{tag}_w_deq"])
+    qa, sa = O.dynamic_per_token_quant(x)
+    np.testing.assert_array_equal(sa, g[f"{tag}_x_dyn_s"])
+    np.testing.assert_array_equal((qa.astype(np.float32) * sa).astype(x.dtype), g[f"{tag}_x_dyn_qdq"])
