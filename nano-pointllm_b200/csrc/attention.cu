@@ -186,6 +186,16 @@ __device__ __forceinline__ void bulk_load(void* smem_dst, const void* src, uint3
                : "memory");
 }
 
+// The same with an L2 cache-eviction policy (createpolicy).
+__device__ __forceinline__ void bulk_load_pol(void* smem_dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                              uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar)), "l"(pol)
+      : "memory");
+}
+
 // Counter increment with acquire-release semantics at GPU scope: the CTA's
 // earlier writes (ordered before this thread by a barrier) are visible to
 // whoever observes the new value, and writes observed here are visible after.
@@ -521,6 +531,383 @@ __global__ void __launch_bounds__(kAttnThreads, kAttnCtasPerSm)
   }
 }
 
+// --------------------------------------- paged decode attention, row streams
+// The kernel for head_dim 128 (the 7B geometry and any H multiple of 4 up to
+// 64). One CTA per SM; a work unit is (64-token chunk of a sequence's
+// context) x EVERY head, so the CTA streams whole cache rows: each token's K
+// (and V) row of all kv heads is contiguous (Hkv x 256 bytes; 8 KB at the 7B
+// geometry), and the tokens of a chunk inside one cache block are contiguous
+// too, so every copy is one 1-D bulk copy of several KB. Units are numbered
+// chunk-major (chunk 0 of every sequence, then chunk 1, ...) and dealt out
+// round-robin, so the light last chunks come last.
+//
+//   warp 0         producer: for each unit, ring stages of tok_stage tokens
+//                  (K rows then V rows, ~32 KB each) by cp.async.bulk
+//   warps 1..      consumers: H/2 warps of 2 q-heads (16 lanes per head, 8
+//                  dims per lane) for H <= 32, else H/4 warps of 4 q-heads
+//                  (8 lanes, 16 dims); a quarter-warp always reads 128
+//                  contiguous bytes (no bank conflicts); one online softmax
+//                  per head over the unit. q . k runs as fp16 x fp16
+//                  products accumulated in fp32 by mixed-precision FMA (the
+//                  fp16 operands need no conversion); p * v in fp32.
+//
+// Every unit ends in a partial (max, sum, acc[D]) per head. A sequence with
+// one unit (context <= 64) is finished right there; otherwise its units write
+// their partials and the unit that completes the sequence (a per-sequence
+// counter) merges all of them in chunk order and writes out[b]. The split of
+// a sequence depends only on its own context length, never on the rest of the
+// batch, so a sequence's result is the same in any batch. With q_out, the
+// CTA that finishes a sequence also quantises its attention row per token
+// (as npl_quant_rows), the O projection's input.
+constexpr int kRowUnit = 64;
+constexpr int kRowMaxWarps = 16;  // consumer warps: H <= 64
+constexpr int kRowStageTarget = 32 * 1024;
+constexpr int kRowSmemBudget = 200 * 1024;
+
+struct RowArgs {
+  const __half* q;
+  int B, H, Hkv;
+  const unsigned char* kc;  // [num_blocks * block_size] rows of row_bytes
+  const unsigned char* vc;
+  int num_blocks, block_size;
+  const int32_t* bt;
+  int bt_stride, max_blocks;
+  const int32_t* ctx_lens;
+  float scale;
+  int n_chunks;   // 64-token units per sequence at most
+  int tok_stage;  // tokens per ring stage (divides 64)
+  int n_stages;
+  int row_bytes;  // Hkv * 128 * 2
+  __half* out;
+  int8_t* q_out;
+  float* q_scale;
+  float* part_ml;   // [B][n_chunks][H][2]
+  float* part_acc;  // [B][n_chunks][H][128]
+  int32_t* cnt;     // [B]: units finished (reset by the unit that merges)
+  int* status;
+};
+
+__device__ __forceinline__ void rows_bar(int nthreads) {
+  asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
+}
+
+__device__ __forceinline__ int rows_ctx(const RowArgs& p, int b) {
+  return min(max(0, p.ctx_lens[b]), p.max_blocks * p.block_size);
+}
+
+
+// An fp16 pair as two fp32 values.
+__device__ __forceinline__ float2 h2f2(uint32_t x) {
+  __half2 h = *reinterpret_cast<__half2*>(&x);
+  return __half22float2(h);
+}
+// d_lo += x.lo * y.lo and d_hi += x.hi * y.hi for fp16 pairs x, y, with the
+// fp16 x fp16 products (exact in fp32) accumulated in fp32 (mixed-precision
+// FMA: no conversion of the fp16 operands to fp32 first).
+__device__ __forceinline__ void fma2_f32_f16(float& d_lo, float& d_hi, uint32_t x, uint32_t y) {
+  asm("{.reg .f16 xl, xh, yl, yh;\n\t"
+      "mov.b32 {xl, xh}, %2;\n\t"
+      "mov.b32 {yl, yh}, %3;\n\t"
+      "fma.rn.f32.f16 %0, xl, yl, %0;\n\t"
+      "fma.rn.f32.f16 %1, xh, yh, %1;}"
+      : "+f"(d_lo), "+f"(d_hi)
+      : "r"(x), "r"(y));
+}
+
+
+// Lane layout of the consumers, for DPL (dims per lane) 8 or 16: a head's
+// 128 dims are spread over LPH = 128 / DPL lanes, each holding DPL / 8
+// 16-byte chunks (chunk c at byte c * 128 + 16 j of the head, j < LPH), so a
+// quarter-warp always reads 128 contiguous bytes; a warp covers HPW = 32 / LPH
+// q-heads.
+template <int DPL>
+struct RowLanes {
+  static constexpr int LPH = 128 / DPL;
+  static constexpr int HPW = 32 / LPH;
+  static constexpr int CH = DPL / 8;  // 16-byte chunks per lane
+};
+
+// The lane's chunks of a cache row (or q row), as DPL / 2 fp16 pairs.
+template <int DPL>
+__device__ __forceinline__ void load_pairs(const unsigned char* row, int off, uint32_t (&v)[DPL / 2]) {
+#pragma unroll
+  for (int c = 0; c < DPL / 8; ++c) {
+    const uint4 a = *reinterpret_cast<const uint4*>(row + off + c * 128);
+    v[4 * c] = a.x;
+    v[4 * c + 1] = a.y;
+    v[4 * c + 2] = a.z;
+    v[4 * c + 3] = a.w;
+  }
+}
+
+// out[b, hq] (and the int8 row of b) from a finished (sum, acc); every
+// consumer thread of the CTA calls it together.
+template <int DPL>
+__device__ void rows_finish(const RowArgs& p, float* red, int nthreads, int cw, int lane, int b, int hq, int j,
+                            float l, const float (&acc)[DPL]) {
+  __half o[DPL];
+#pragma unroll
+  for (int i = 0; i < DPL; ++i) o[i] = __float2half_rn(l > 0.f ? acc[i] / l : 0.f);
+  __half* orow = p.out + ((size_t)b * p.H + hq) * 128;
+#pragma unroll
+  for (int c = 0; c < DPL / 8; ++c)
+    *reinterpret_cast<uint4*>(orow + 64 * c + 8 * j) = *reinterpret_cast<const uint4*>(&o[8 * c]);
+  if (!p.q_out) return;
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < DPL; ++i) amax = fmaxf(amax, fabsf(__half2float(o[i])));
+  amax = warp_max(amax);
+  if (lane == 0) red[cw] = amax;
+  rows_bar(nthreads);
+  amax = 0.f;
+  for (int i = 0; i < nthreads / 32; ++i) amax = fmaxf(amax, red[i]);
+  const float sc = scale_from_absmax(amax);
+  const float rsc = quant_recip(sc);
+  int8_t* qrow = p.q_out + ((size_t)b * p.H + hq) * 128;
+#pragma unroll
+  for (int c = 0; c < DPL / 8; ++c) {
+    uint2 u;
+    uint32_t* w = reinterpret_cast<uint32_t*>(&u);
+    w[0] = w[1] = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      w[i / 4] |= (uint32_t)(quantize_one(__half2float(o[8 * c + i]), sc, rsc) & 0xff) << (8 * (i % 4));
+    *reinterpret_cast<uint2*>(qrow + 64 * c + 8 * j) = u;
+  }
+  if (cw == 0 && lane == 0) p.q_scale[b] = sc;
+  rows_bar(nthreads);  // red[] is free again
+}
+
+template <int DPL>
+__global__ void __launch_bounds__(32 * (kRowMaxWarps + 1), 1) decode_attn_rows_kernel(const RowArgs p) {
+  using LN = RowLanes<DPL>;
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) &
+                                                         ~uintptr_t(127));
+  const int nw = (int)(blockDim.x >> 5) - 1;  // consumer warps
+  const int nthreads = nw * 32;
+  const size_t stage_bytes = (size_t)p.tok_stage * p.row_bytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + 2 * (size_t)p.n_stages * stage_bytes);
+  uint64_t* empty = full + p.n_stages;
+  int4* meta = reinterpret_cast<int4*>(empty + p.n_stages);
+  float* red = reinterpret_cast<float*>(meta + p.n_stages);
+  int* merge_flag = reinterpret_cast<int*>(red + kRowMaxWarps);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < p.n_stages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], nw);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+  pdl_trigger();
+  pdl_wait();
+  const int n_units = p.n_chunks * p.B;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------- producer
+    if (lane != 0) return;
+    const uint64_t pol = policy_evict_first();
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t used = 0, parity = 0;  // per ring slot: issued at least once; parity of its last phase
+    bool ok = true;
+    for (int u = (int)blockIdx.x; u < n_units && ok; u += (int)gridDim.x) {
+      const int chunk = u / p.B, b = u % p.B;
+      const int ctx = rows_ctx(p, b);
+      const int n_b = max(1, (ctx + kRowUnit - 1) / kRowUnit);
+      if (chunk >= n_b) continue;
+      const int t0 = chunk * kRowUnit, t_end = min(ctx, t0 + kRowUnit);
+      const int n_st = max(1, (t_end - t0 + p.tok_stage - 1) / p.tok_stage);
+      const int32_t* table = p.bt + (size_t)b * p.bt_stride;
+      for (int st = 0; st < n_st; ++st) {
+        const int tok0 = t0 + st * p.tok_stage;
+        int valid = max(0, min(p.tok_stage, t_end - tok0));
+        // pieces: runs of the stage's tokens inside one cache block (at most
+        // 64 / 8: block_size >= 8, tok_stage <= 64)
+        const int piece = min(p.tok_stage, p.block_size);
+        long long rows[kRowUnit / 8];
+        int n_pieces = min((valid + piece - 1) / piece, kRowUnit / 8);
+        for (int i = 0; i < n_pieces; ++i) {
+          const int tok = tok0 + i * piece;
+          const int blk = table[tok / p.block_size];
+          if (blk < 0 || blk >= p.num_blocks) {
+            atomicCAS(p.status, 0, kDevBadIndex);
+            valid = 0;  // the stage is skipped (its tokens count as masked)
+            n_pieces = 0;
+            break;
+          }
+          rows[i] = (long long)blk * p.block_size + tok % p.block_size;
+        }
+        if (!mbar_wait(&empty[stage], phase ^ 1, p.status, NPL_DEV_TIMEOUT_TMA)) {
+          ok = false;
+          break;
+        }
+        meta[stage] = make_int4(u, st, valid, st == n_st - 1);
+        used |= 1u << stage;
+        parity = (parity & ~(1u << stage)) | (phase << stage);
+        mbar_arrive_expect_tx(&full[stage], 2u * (uint32_t)valid * (uint32_t)p.row_bytes);
+        unsigned char* kdst = smem + (size_t)(2 * stage) * stage_bytes;
+        unsigned char* vdst = kdst + stage_bytes;
+        for (int i = 0; i < n_pieces; ++i) {
+          const int ntok = min(piece, valid - i * piece);
+          const uint32_t bytes = (uint32_t)ntok * (uint32_t)p.row_bytes;
+          const size_t src = (size_t)rows[i] * p.row_bytes;
+          const size_t dst = (size_t)i * piece * p.row_bytes;
+          bulk_load_pol(kdst + dst, p.kc + src, bytes, &full[stage], pol);
+          bulk_load_pol(vdst + dst, p.vc + src, bytes, &full[stage], pol);
+        }
+        if (++stage == p.n_stages) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+    }
+    if (ok && mbar_wait(&empty[stage], phase ^ 1, p.status, NPL_DEV_TIMEOUT_TMA)) {
+      meta[stage] = make_int4(-1, 0, 0, 0);
+      used |= 1u << stage;
+      parity = (parity & ~(1u << stage)) | (phase << stage);
+      mbar_arrive(&full[stage]);
+    }
+    // Copies land before the CTA exits: the last phase of every slot that was
+    // issued has completed (at once, unless a wait above expired).
+    for (int i = 0; i < p.n_stages; ++i)
+      if (used >> i & 1) mbar_wait(&full[i], parity >> i & 1, p.status, NPL_DEV_TIMEOUT_TEARDOWN);
+    return;
+  }
+
+  // ------------------------------------------------------------- consumers
+  const int cw = warp - 1;
+  const int hq = cw * LN::HPW + lane / LN::LPH;  // q-head of this lane
+  const int j = lane % LN::LPH;                  // chunk c covers dims 64 c + 8 j .. + 8
+  const int kvh = hq / (p.H / p.Hkv);
+  const int koff = kvh * 256 + j * 16;  // byte offset of the lane's first chunk in a cache row
+  const float qscale = p.scale * 1.4426950408889634f;  // scores in log2 units
+  uint32_t qv[DPL / 2];  // the lane's query values, fp16 pairs (scaled after the dot)
+  float acc[DPL];        // the same dims, in pair order
+  float m = kNegBig, l = 0.f;
+  int stage = 0;
+  uint32_t phase = 0;
+  while (true) {
+    if (!mbar_wait(&full[stage], phase, p.status, NPL_DEV_TIMEOUT_EPILOGUE)) break;
+    const volatile int* mv = reinterpret_cast<volatile int*>(&meta[stage]);
+    const int4 mt = make_int4(mv[0], mv[1], mv[2], mv[3]);
+    if (mt.x < 0) break;
+    const int chunk = mt.x / p.B, b = mt.x % p.B;
+    if (mt.y == 0) {
+      const unsigned char* qrow = reinterpret_cast<const unsigned char*>(p.q + ((size_t)b * p.H + hq) * 128);
+#pragma unroll
+      for (int c = 0; c < LN::CH; ++c) {
+        const uint4 a = __ldcg(reinterpret_cast<const uint4*>(qrow + c * 128 + j * 16));
+        qv[4 * c] = a.x;
+        qv[4 * c + 1] = a.y;
+        qv[4 * c + 2] = a.z;
+        qv[4 * c + 3] = a.w;
+      }
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) acc[i] = 0.f;
+      m = kNegBig;
+      l = 0.f;
+    }
+    const unsigned char* ks = smem + (size_t)(2 * stage) * stage_bytes;
+    const unsigned char* vs = ks + stage_bytes;
+    for (int t0 = 0; t0 < mt.z; t0 += 4) {
+      float sc[4];
+      float mnew = m;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int t = min(t0 + u, mt.z - 1);
+        uint32_t kv[DPL / 2];
+        load_pairs<DPL>(ks + (size_t)t * p.row_bytes, koff, kv);
+        float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;  // four chains of q . k over the lane's dims
+#pragma unroll
+        for (int i = 0; i < DPL / 2; i += 2) {
+          fma2_f32_f16(d0, d1, qv[i], kv[i]);
+          fma2_f32_f16(d2, d3, qv[i + 1], kv[i + 1]);
+        }
+        float d = (d0 + d1) + (d2 + d3);
+#pragma unroll
+        for (int o = LN::LPH / 2; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+        sc[u] = t0 + u < mt.z ? d * qscale : -INFINITY;
+        mnew = fmaxf(mnew, sc[u]);
+      }
+      const float alpha = exp2f(m - mnew);
+      l *= alpha;
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) acc[i] *= alpha;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (t0 + u < mt.z) {
+          const float pu = exp2f(sc[u] - mnew);
+          l += pu;
+          
+          uint32_t vv[DPL / 2];
+          load_pairs<DPL>(vs + (size_t)(t0 + u) * p.row_bytes, koff, vv);
+#pragma unroll
+          for (int i = 0; i < DPL / 2; ++i) {
+            const float2 f = h2f2(vv[i]);
+            acc[2 * i] = fmaf(pu, f.x, acc[2 * i]);
+            acc[2 * i + 1] = fmaf(pu, f.y, acc[2 * i + 1]);
+          }
+        }
+      }
+      m = mnew;
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[stage]);
+    if (++stage == p.n_stages) {
+      stage = 0;
+      phase ^= 1;
+    }
+    if (!mt.w) continue;
+
+    // ---- end of a unit
+    const int n_b = max(1, (rows_ctx(p, b) + kRowUnit - 1) / kRowUnit);
+    if (n_b == 1) {
+      rows_finish<DPL>(p, red, nthreads, cw, lane, b, hq, j, l, acc);
+      continue;
+    }
+    const size_t pi = ((size_t)b * p.n_chunks + chunk) * p.H + hq;
+    if (j == 0) __stcg(reinterpret_cast<float2*>(p.part_ml) + pi, make_float2(m, l));
+    float4* pa = reinterpret_cast<float4*>(p.part_acc + pi * 128);
+#pragma unroll
+    for (int c = 0; c < LN::CH; ++c) {
+      __stcg(pa + 16 * c + 2 * j, make_float4(acc[8 * c], acc[8 * c + 1], acc[8 * c + 2], acc[8 * c + 3]));
+      __stcg(pa + 16 * c + 2 * j + 1, make_float4(acc[8 * c + 4], acc[8 * c + 5], acc[8 * c + 6], acc[8 * c + 7]));
+    }
+    rows_bar(nthreads);  // every partial write of the CTA before the count (cumulative release)
+    if (cw == 0 && lane == 0) *merge_flag = atomic_add_acq_rel(p.cnt + b, 1) + 1 == n_b;
+    rows_bar(nthreads);
+    if (!*merge_flag) continue;
+    // this unit completes sequence b: merge its partials in chunk order
+    float mm = kNegBig, ll = 0.f, aa[DPL];
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) aa[i] = 0.f;
+    for (int cidx = 0; cidx < n_b; ++cidx) {
+      const size_t pc = ((size_t)b * p.n_chunks + cidx) * p.H + hq;
+      const float2 ml = __ldcg(reinterpret_cast<const float2*>(p.part_ml) + pc);
+      const float4* src = reinterpret_cast<const float4*>(p.part_acc + pc * 128);
+      float ac[DPL];
+#pragma unroll
+      for (int c = 0; c < LN::CH; ++c) {
+        const float4 x0 = __ldcg(src + 16 * c + 2 * j), x1 = __ldcg(src + 16 * c + 2 * j + 1);
+        ac[8 * c] = x0.x; ac[8 * c + 1] = x0.y; ac[8 * c + 2] = x0.z; ac[8 * c + 3] = x0.w;
+        ac[8 * c + 4] = x1.x; ac[8 * c + 5] = x1.y; ac[8 * c + 6] = x1.z; ac[8 * c + 7] = x1.w;
+      }
+      const float mn = fmaxf(mm, ml.x);
+      const float w0 = exp2f(mm - mn), w1 = exp2f(ml.x - mn);
+      ll = ll * w0 + ml.y * w1;
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) aa[i] = aa[i] * w0 + ac[i] * w1;
+      mm = mn;
+    }
+    if (cw == 0 && lane == 0) p.cnt[b] = 0;  // no other unit of this launch counts b again
+    rows_finish<DPL>(p, red, nthreads, cw, lane, b, hq, j, ll, aa);
+  }
+}
+
 // fp16 cache [num_blocks * block_size][Hkv][D] as a 3-D tensor map; box =
 // (D, 1 head, box_tok tokens).
 int make_cache_map(CUtensorMap* map, const void* base, int num_blocks, int block_size, int Hkv, int D, int box_tok) {
@@ -555,10 +942,16 @@ struct AttnLayout {
   size_t work, cnt_row, flags, ml, acc, total;
 };
 
+// The partials are sized for both kernels: (sequence, head, 256-token chunk)
+// of decode_attn_kernel and (sequence, 64-token unit, head) of
+// decode_attn_rows_kernel; the per-sequence counters are shared (both leave
+// them zero).
 AttnLayout attn_layout(int B, int H, int D, int max_blocks, int block_size) {
   auto al = [](size_t x) { return (x + 255) & ~size_t(255); };
-  const size_t n_chunks = std::max<size_t>(1, ((size_t)max_blocks * block_size + kAttnChunk - 1) / kAttnChunk);
-  const size_t parts = (size_t)B * H * n_chunks;
+  const size_t ctx = (size_t)max_blocks * block_size;
+  const size_t n_chunks = std::max<size_t>(1, (ctx + kAttnChunk - 1) / kAttnChunk);
+  const size_t n_units = std::max<size_t>(1, (ctx + kRowUnit - 1) / kRowUnit);
+  const size_t parts = std::max((size_t)B * H * n_chunks, (size_t)B * H * n_units);
   AttnLayout l;
   l.work = 0;
   l.cnt_row = 256;
@@ -567,6 +960,30 @@ AttnLayout attn_layout(int B, int H, int D, int max_blocks, int block_size) {
   l.acc = l.ml + al(parts * 2 * sizeof(float));
   l.total = l.acc + al(parts * D * sizeof(float));
   return l;
+}
+
+// Ring configuration of decode_attn_rows_kernel for this geometry (0 stages:
+// not supported, use decode_attn_kernel).
+struct RowConfig {
+  int tok_stage, n_stages, row_bytes, warps;
+  size_t smem;
+};
+
+// Consumer layout: 8 dims per lane (2 q-heads per warp) while H / 2 warps fit,
+// else 16 dims per lane (4 q-heads per warp).
+RowConfig row_config(int H, int Hkv, int D, int block_size) {
+  RowConfig c{0, 0, Hkv * D * 2, H % 2 == 0 && H / 2 <= kRowMaxWarps ? H / 2 : H / 4, 0};
+  if (D != 128 || H % 4 || H / 4 > kRowMaxWarps || H % Hkv) return c;
+  int t = kRowUnit;
+  while (t > 1 && (size_t)t * c.row_bytes > kRowStageTarget) t /= 2;
+  if (block_size % t && t % block_size) return c;
+  const size_t stage = (size_t)t * c.row_bytes;
+  const int n = (int)std::min<size_t>(4, kRowSmemBudget / (2 * stage));
+  if (n < 2) return c;
+  c.tok_stage = t;
+  c.n_stages = n;
+  c.smem = 128 + 2 * (size_t)n * stage + n * (2 * sizeof(uint64_t) + sizeof(int4)) + kRowMaxWarps * sizeof(float) + 16;
+  return c;
 }
 
 }  // namespace
@@ -646,6 +1063,43 @@ extern "C" int npl_paged_decode_attention(const void* q, int B, int H, int Hkv, 
   const AttnLayout lay = attn_layout(B, H, D, max_blocks, block_size);
   if (!workspace || workspace_bytes < lay.total || !aligned16(workspace))
     return fail(NPL_ERR_ARG, "npl_paged_decode_attention: workspace of %zu bytes required", lay.total);
+  const RowConfig rc = row_config(H, Hkv, D, block_size);
+  if (rc.n_stages > 0) {
+    char* ws = static_cast<char*>(workspace);
+    RowArgs r{};
+    r.q = static_cast<const __half*>(q);
+    r.B = B;
+    r.H = H;
+    r.Hkv = Hkv;
+    r.kc = static_cast<const unsigned char*>(k_cache);
+    r.vc = static_cast<const unsigned char*>(v_cache);
+    r.num_blocks = num_blocks;
+    r.block_size = block_size;
+    r.bt = block_tables;
+    r.bt_stride = bt_stride;
+    r.max_blocks = max_blocks;
+    r.ctx_lens = context_lens;
+    r.scale = scale;
+    r.n_chunks = std::max(1, (max_blocks * block_size + kRowUnit - 1) / kRowUnit);
+    r.tok_stage = rc.tok_stage;
+    r.n_stages = rc.n_stages;
+    r.row_bytes = rc.row_bytes;
+    r.out = static_cast<__half*>(out);
+    r.q_out = q_out;
+    r.q_scale = q_scale;
+    r.part_ml = reinterpret_cast<float*>(ws + lay.ml);
+    r.part_acc = reinterpret_cast<float*>(ws + lay.acc);
+    r.cnt = reinterpret_cast<int32_t*>(ws + lay.cnt_row);
+    r.status = device_status_ptr();
+    const int sms = num_sms();
+    const long long units = (long long)r.n_chunks * B;
+    const int grid = (int)std::min<long long>(sms > 0 ? sms : 148, units);
+    auto kern = rc.warps * 2 == H ? decode_attn_rows_kernel<8> : decode_attn_rows_kernel<16>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rc.smem) != cudaSuccess)
+      return launch_status("npl_paged_decode_attention: smem attribute");
+    return launch_pdl("npl_paged_decode_attention", kern, dim3(grid), dim3(32 * (rc.warps + 1)), rc.smem,
+                      static_cast<cudaStream_t>(stream), r);
+  }
   const int box_tok = std::min(kAttnTok, block_size);
   CUtensorMap tk, tv;
   if (int rc = make_cache_map(&tk, k_cache, num_blocks, block_size, Hkv, D, box_tok)) return rc;

@@ -394,3 +394,37 @@ def test_decode_attention_fused_quant_equals_quant_rows(K):
         assert torch.equal(qs, ref_s.reshape(-1))
     assert float(out[2].abs().sum()) == 0.0
     K.lib.device_status()
+
+
+@pytest.mark.parametrize("h,hkv,bs,ctx", [(4, 4, 16, [38, 65, 21]), (32, 32, 256, [1025, 1, 0, 700])])
+def test_decode_attention_right_after_rope_store(K, h, hkv, bs, ctx):
+    """The runner's order: RoPE + KV store writes q and the new token's K/V,
+    then the attention (launched early behind it) reads them, with the fused
+    per-token quantisation; against the oracle on the same q and pool."""
+    from nanopointllm_b200 import synthetic as S
+    d, b = 128, len(ctx)
+    gen = torch.Generator().manual_seed(h + bs)
+    mb = max(1, max(-(-n // bs) for n in ctx)) + 1
+    nb = b * mb + 2
+    bt = S.permuted_block_tables(b, mb, nb, seed=bs).to(K.dev)
+    kc = torch.randn(nb, bs, hkv, d, generator=gen).half().to(K.dev)
+    vc = torch.randn(nb, bs, hkv, d, generator=gen).half().to(K.dev)
+    qkv = torch.randn(b, (h + 2 * hkv) * d, generator=gen).half().to(K.dev)
+    from nanopointllm_b200.rope import rope_tables
+    cos, sin = rope_tables(d, 4096, 10000.0, K.dev)
+    ctx_t = torch.tensor(ctx, dtype=torch.int32, device=K.dev)
+    pos = (ctx_t.long() - 1).clamp_min(0)
+    slots = torch.tensor([int(bt[i, max(n - 1, 0) // bs]) * bs + max(n - 1, 0) % bs if n > 0 else -1
+                          for i, n in enumerate(ctx)], dtype=torch.int32, device=K.dev)
+    for _ in range(2):
+        q = K.PA.rope_store_kvcache(qkv, h, hkv, d, cos, sin, pos, slots, kc, vc)
+        q8 = torch.empty((b, h * d), dtype=torch.int8, device=K.dev)
+        qs = torch.empty((b,), dtype=torch.float32, device=K.dev)
+        out = K.PA.paged_decode_attention(q, kc, vc, bt, ctx_t, d ** -0.5, h // hkv, quant_out=(q8, qs))
+        torch.cuda.synchronize()
+        ref = O.paged_decode_attention(cpu(q), cpu(kc), cpu(vc), cpu(bt), ctx, d ** -0.5, h // hkv)
+        np.testing.assert_allclose(cpu(out).astype(np.float64), ref, atol=2e-3, rtol=2e-3)
+        ref_q, ref_s = K.W.dynamic_per_token_quant(out.reshape(b, -1))
+        assert torch.equal(q8, ref_q)
+        assert torch.equal(qs, ref_s.reshape(-1))
+    K.lib.device_status()
