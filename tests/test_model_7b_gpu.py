@@ -90,6 +90,9 @@ def _recorder(device):
         if fn is W.linear_q:
             acc = torch.empty((a[0].shape[0], a[2].shape[0]), dtype=torch.int32, device=device)
             kw = dict(kw, acc_out=acc)
+        elif fn is W.linear_ex:
+            acc = torch.empty((kw["m"], a[0].shape[0]), dtype=torch.int32, device=device)
+            kw = dict(kw, acc_out=acc)
         out = fn(*a, **kw)
         rec.append((name, a, kw, out, acc))
         return out
@@ -97,20 +100,71 @@ def _recorder(device):
     return rec, timer
 
 
-def _check_layer(li, layer, ops, shape, cos, sin, slots_np, attention):
-    """One decoder layer checked op by op on the GPU's own input to it.
-    ``attention(q_rot_gpu, kc, vc, q_rot_oracle)`` -> (kernel fp16 rows [T,
-    H*D] as run through the library, oracle rows float64 [T, H*D]). Returns
-    (max |attention error|, int8 flips, int8 elements) of the attention rows
-    quantised from the oracle's attention against the kernel's."""
+def _parse(rec, n_layers: int):
+    """Per-layer tensors of a recorded forward, in either op structure of
+    the runner: nine kernels per layer (RMSNorm+quant, QKV, RoPE + KV store,
+    attention, O, RMSNorm+quant, gate/up, quant, down; then the final norm
+    and the LM head), or the decode structure whose O, gate/up and down also
+    produce the next linear's int8 input (next_q / next_scale): one
+    RMSNorm+quant before layer 0, six kernels per layer, the LM head."""
+    names = [r[0] for r in rec]
+    fused = "quant" not in names
+    per = ["linear.qkv", "rope_store", "attention", "linear.o", "linear.gate_up", "linear.down"] if fused else \
+        ["rmsnorm_quant", "linear.qkv", "rope_store", "attention", "linear.o", "rmsnorm_quant", "linear.gate_up",
+         "quant", "linear.down"]
+    want = (["rmsnorm_quant"] + per * n_layers + ["linear.lm_head"]) if fused else \
+        (per * n_layers + ["rmsnorm_quant", "linear.lm_head"])
+    assert names == want, names
+    it = iter(rec)
+    layers, nxt = [], None
+    if fused:
+        _, a, _, (xq, xs, _), _ = next(it)
+        nxt = dict(h=a[0], xq=xq, xs=xs)
+    for _ in range(n_layers):
+        L = {}
+        if fused:
+            L.update(nxt)
+        else:
+            _, a, _, (xq, xs, _), _ = next(it)
+            L.update(h=a[0], xq=xq, xs=xs)
+        _, _, _, L["qkv"], L["qkv_acc"] = next(it)
+        _, _, _, L["q_rot"], _ = next(it)
+        _, _, _, (L["aq"], L["asc"]), _ = next(it)
+        _, _, kw, L["h2"], L["o_acc"] = next(it)
+        if fused:
+            L["xq2"], L["xs2"] = kw["next_q"], kw["next_scale"]
+        else:
+            _, _, _, (L["xq2"], L["xs2"], _), _ = next(it)
+        _, _, kw, L["act"], L["gu_acc"] = next(it)
+        if fused:
+            L["mq"], L["ms"] = kw["next_q"], kw["next_scale"]
+        else:
+            _, _, _, (L["mq"], L["ms"]), _ = next(it)
+        _, _, kw, L["h_next"], L["d_acc"] = next(it)
+        if fused:
+            nxt = dict(h=L["h_next"], xq=kw["next_q"], xs=kw["next_scale"])
+        layers.append(L)
+    if fused:
+        final = dict(nxt)
+    else:
+        _, a, _, (xq, xs, _), _ = next(it)
+        final = dict(h=a[0], xq=xq, xs=xs)
+    _, _, _, final["logits"], final["lm_acc"] = next(it)
+    return layers, final
+
+
+def _check_layer(li, layer, L, shape, cos, sin, slots_np, attention):
+    """One decoder layer (tensors from _parse) checked op by op on the GPU's
+    own input to it. ``attention(q_rot_gpu, layer, kc, vc, q_rot_oracle)`` ->
+    (kernel fp16 rows [T, H*D] as run through the library, oracle rows
+    float64 [T, H*D]). Returns (max |attention error|, int8 flips, int8
+    elements) of the attention rows quantised from the oracle's attention
+    against the kernel's."""
     H, D, inter = shape.heads, shape.head_dim, shape.intermediate
-    names = [o[0] for o in ops]
-    assert names == ["rmsnorm_quant", "linear.qkv", "rope_store", "attention", "linear.o", "rmsnorm_quant",
-                     "linear.gate_up", "quant", "linear.down"], names
-    (_, a0, _, (xq, xs, _), _), (_, _, _, qkv, qkv_acc), (_, _, _, q_rot, _), (_, _, _, (aq, asc), _), \
-        (_, _, _, h2, o_acc), (_, _, _, (xq2, xs2, _), _), (_, _, _, act, gu_acc), (_, _, _, (mq, ms), _), \
-        (_, _, _, h_next, d_acc) = ops
-    h = cpu(a0[0])
+    xq, xs, qkv, qkv_acc, q_rot = L["xq"], L["xs"], L["qkv"], L["qkv_acc"], L["q_rot"]
+    aq, asc, h2, o_acc, xq2, xs2 = L["aq"], L["asc"], L["h2"], L["o_acc"], L["xq2"], L["xs2"]
+    act, gu_acc, mq, ms, h_next, d_acc = L["act"], L["gu_acc"], L["mq"], L["ms"], L["h_next"], L["d_acc"]
+    h = cpu(L["h"])
     T = h.shape[0]
     msg = f"layer {li}"
     # input RMSNorm + quantisation
@@ -215,7 +269,7 @@ def test_7b_decode_step_every_layer(cuda_device):
         R.clear_forward_context()
         run.timer = None
     torch.cuda.synchronize()
-    assert len(rec) == 9 * shape.layers + 2
+    layers_rec, final = _parse(rec, shape.layers)
 
     H, D = shape.heads, shape.head_dim
     pos_np = cpu(positions)
@@ -231,12 +285,12 @@ def test_7b_decode_step_every_layer(cuda_device):
 
     attn_err, int8_flips, int8_total = 0.0, 0, 0
     for li, layer in enumerate(run.layers):
-        e, f, n = _check_layer(li, layer, rec[9 * li: 9 * li + 9], shape, cos, sin, slots_np, attention)
+        e, f, n = _check_layer(li, layer, layers_rec[li], shape, cos, sin, slots_np, attention)
         attn_err, int8_flips, int8_total = max(attn_err, e), int8_flips + f, int8_total + n
 
     # final norm, LM head (N = 32003), greedy token
-    (_, a0, _, (fq, fs, _), _), (_, _, _, lg, lm_acc) = rec[-2:]
-    oq, osc, _, _ = O.rmsnorm_quant(cpu(a0[0]), cpu(run.norm), shape.eps)
+    fq, fs, lm_acc = final["xq"], final["xs"], final["lm_acc"]
+    oq, osc, _, _ = O.rmsnorm_quant(cpu(final["h"]), cpu(run.norm), shape.eps)
     np.testing.assert_array_equal(cpu(fq), oq)
     np.testing.assert_array_equal(cpu(fs), osc)
     acc = O.int_matmul_nt(oq, cpu(run.lm_head.qweight))
@@ -352,12 +406,13 @@ def test_7b_prefill_every_op(cuda_device):
                                         np.arange(BATCH) * CTX, D ** -0.5, 1, block_n=128)
         return cpu(att).reshape(-1, H * D), ref.astype(np.float64).reshape(-1, H * D)
 
+    layers_rec, final = _parse(rec, shape.layers)
     stats = []
     for li, layer in enumerate(run.layers):
-        stats.append(_check_layer(li, layer, rec[9 * li: 9 * li + 9], shape, cos, sin, slots_np, attention))
+        stats.append(_check_layer(li, layer, layers_rec[li], shape, cos, sin, slots_np, attention))
     # final norm of each sequence's last row, LM head
-    (_, a0, _, (fq, fs, _), _), (_, _, _, lg, lm_acc) = rec[-2:]
-    oq, osc, _, _ = O.rmsnorm_quant(cpu(a0[0]), cpu(run.norm), shape.eps)
+    fq, lm_acc = final["xq"], final["lm_acc"]
+    oq, osc, _, _ = O.rmsnorm_quant(cpu(final["h"]), cpu(run.norm), shape.eps)
     np.testing.assert_array_equal(cpu(fq), oq)
     acc = O.int_matmul_nt(oq, cpu(run.lm_head.qweight))
     np.testing.assert_array_equal(cpu(lm_acc), acc)
