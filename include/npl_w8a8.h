@@ -246,9 +246,10 @@ int npl_w8a8_linear_ex(const npl_linear_args* args, void* workspace, size_t work
  * until the process exits): M <= 64 tokens on devices with at most 160 SMs;
  * larger M is rejected with NPL_ERR_ARG. Every call shares that array: calls
  * that overlap on the GPU (other streams, other host threads) race and give
- * wrong results. Each call clears the part it uses on its stream first. The
- * first call on a device looks up the array's address; make it before any
- * stream capture.
+ * wrong results. Each call clears the part it uses on its stream first. A
+ * call outside stream capture looks up the array's address on the current
+ * device; a call during capture reuses the last one, so make the first call
+ * on each device before any stream capture.
  */
 int npl_w8a8_linear_noalloc(const int8_t* qa, int lda, const float* sa, const int8_t* qw, int ldw,
                             const float* sw, const float* bias_or_null, int M, int N, int K, int epilogue,

@@ -49,6 +49,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <atomic>
 #include <initializer_list>
 #include <mutex>
 #include <vector>
@@ -1421,9 +1422,12 @@ extern "C" int npl_w8a8_linear_ex(const npl_linear_args* args, void* workspace, 
 // different streams, or in different host threads) race on it and give wrong
 // results. Each call zeroes the part it uses (on the caller's stream) before
 // the kernel runs, so a call never depends on what an earlier call left there.
-// The first call on each device looks up the array's device address with
-// cudaGetSymbolAddress (with that device current); make that first call
-// before starting any stream capture.
+// Every call outside stream capture looks up the array's device address with
+// cudaGetSymbolAddress (with the device current); a call during capture uses
+// the address of the device's last lookup, so make the first call on each
+// device before starting any stream capture. Clearing the scratch is one
+// cudaMemsetAsync of ws_bytes(M) (at most ~5 MiB at M = 64) on the caller's
+// stream per call, a launch of its own ahead of the linear.
 // ----------------------------------------------------------------------------
 namespace npl {
 namespace {
@@ -1436,22 +1440,31 @@ constexpr size_t kNoAllocBytes = kNoAllocAccBytes + ((kNoAllocMaxSlots * sizeof(
 static __device__ __align__(256) unsigned char g_linear_scratch[kNoAllocBytes];
 
 constexpr int kNoAllocDevices = 64;
-void* g_scratch_ptr[kNoAllocDevices];
+std::atomic<void*> g_scratch_ptr[kNoAllocDevices];
 
-// Device address of g_linear_scratch on the current device (looked up once).
-int scratch_address(void** out) {
+// Device address of g_linear_scratch on the current device. Outside stream
+// capture it is looked up on every call (cudaGetSymbolAddress is a host-side
+// query, and a fresh lookup stays right after a device reset reloads the
+// module); during capture the address of the last lookup on this device is
+// used, so a device's first call must come before any capture. The cache
+// entries are atomic: host threads may call concurrently.
+int scratch_address(cudaStream_t stream, void** out) {
   int dev = -1;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocDevices)
     return fail(NPL_ERR_LAUNCH, "npl_w8a8_linear_noalloc: no usable current device");
-  if (!g_scratch_ptr[dev]) {
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess)
+    return launch_status("npl_w8a8_linear_noalloc: stream capture status");
+  if (cap == cudaStreamCaptureStatusNone) {
     void* p = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&p, g_linear_scratch);
     if (e != cudaSuccess || !p)
-      return fail(NPL_ERR_LAUNCH, "npl_w8a8_linear_noalloc: cudaGetSymbolAddress failed: %s",
-                  cudaGetErrorString(e));
-    g_scratch_ptr[dev] = p;
+      return fail(NPL_ERR_LAUNCH, "npl_w8a8_linear_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+    g_scratch_ptr[dev].store(p, std::memory_order_release);
   }
-  *out = g_scratch_ptr[dev];
+  *out = g_scratch_ptr[dev].load(std::memory_order_acquire);
+  if (!*out)
+    return fail(NPL_ERR_ARG, "npl_w8a8_linear_noalloc: the first call on a device must come before stream capture");
   return NPL_OK;
 }
 
@@ -1478,7 +1491,7 @@ extern "C" int npl_w8a8_linear_noalloc(const int8_t* qa, int lda, const float* s
                 "(more than %d SMs)",
                 need, npl::kNoAllocBytes, npl::kNoAllocMaxSlots + 1);
   void* scratch = nullptr;
-  if (int rc = npl::scratch_address(&scratch)) return rc;
+  if (int rc = npl::scratch_address(static_cast<cudaStream_t>(stream), &scratch)) return rc;
   if (cudaMemsetAsync(scratch, 0, need, static_cast<cudaStream_t>(stream)) != cudaSuccess)
     return launch_status("npl_w8a8_linear_noalloc: clearing the scratch");
   return npl_w8a8_linear(qa, lda, sa, qw, ldw, sw, bias, M, N, K, epilogue, residual, ld_res, out, ld_out,

@@ -117,9 +117,9 @@ __device__ __forceinline__ float scale_from_absmax(float absmax) {
 // They are whenever the result can differ from 0: s >= 2^-14 is normal, and
 // |v / s| >= 1/2 makes |v| >= 2^-15 and |e| >= ulp(q1 s) / 2 >= 2^-40; for
 // |v / s| < 1/2 the rounded integer is 0 either way (q stays below 1/2 or
-// rounds to it, and rint(+-1/2) = 0). The scales are fp16 values, so the
-// pairs (fp16 v, scale) are checked exhaustively against IEEE division by
-// the tests, and fp32 v by sampling.
+// rounds to it, and rint(+-1/2) = 0). The tests check every finite fp16 v
+// against IEEE division for ~200 scales spread over the fp16 range (the
+// scales are fp16 values), and fp32 v by sampling.
 __device__ __forceinline__ float quant_recip(float s) { return __frcp_rn(s); }
 
 __device__ __forceinline__ int quantize_one(float v, float s, float r) {

@@ -28,7 +28,7 @@
 // call parity: a rank can be at most one call ahead of a peer (it cannot pass
 // call n + 1 before every peer has started it, which needs the peer's call n
 // to have finished), so a slot is never overwritten while it is being read.
-// No TMA and no multicast: only plain loads and stores.
+// No TMA and no bulk copies: only plain loads and stores.
 #include <algorithm>
 #include <cstring>
 

@@ -1,4 +1,4 @@
-"""Tensor-parallel host logic on CPU: world size 2 over gloo (127.0.0.1).
+"""Tensor-parallel host logic on CPU: world sizes 2 and 4 over gloo (127.0.0.1).
 
 Each rank slices oracle-quantised full weights with the plan of
 nanopointllm_b200.tp (the functions the GPU runner uses), runs its part of a
@@ -37,7 +37,10 @@ def _rank_main(rank: int, world: int, port: int, errors) -> None:
         from nanopointllm_b200 import tp
         from nanopointllm_b200.synthetic import LlamaShape
 
-        shape = LlamaShape(hidden=256, heads=4, kv_heads=2, head_dim=64, intermediate=336, layers=1, vocab=1001)
+        # world 4 also leaves a rank's intermediate slice ragged (344 = 4 x 86)
+        shape = LlamaShape(hidden=256, heads=4, kv_heads=2, head_dim=64, intermediate=336, layers=1, vocab=1001) \
+            if world == 2 else LlamaShape(hidden=256, heads=8, kv_heads=4, head_dim=64, intermediate=344, layers=1,
+                                          vocab=1001)
         plan = tp.tp_plan(shape, rank, world)
         rng = np.random.default_rng(7)  # same full weights on every rank
         m, hd = 5, shape.head_dim
@@ -118,8 +121,8 @@ def _rank_main(rank: int, world: int, port: int, errors) -> None:
         errors.put(f"rank {rank}: {e!r}\n{traceback.format_exc()}")
 
 
-def test_tp_sharding_and_exchanges_world2():
-    world = 2
+@pytest.mark.parametrize("world", [2, 4])
+def test_tp_sharding_and_exchanges(world):
     ctx = mp.get_context("spawn")
     errors = ctx.SimpleQueue()
     port = _free_port()
