@@ -651,7 +651,7 @@ def run_kernel_case(args, torch, device) -> dict:
         us = timed(lambda i: PA.paged_decode_attention(q, sets[i % 3][0], sets[i % 3][1], bt, cl, shape.head_dim ** -0.5,
                                                         1, out=out, quant_out=(q8, qs)), 1)
         nbytes = op_bytes(shape, "attention", ctx_len)
-        line.update({"kernel": "decode_attn_kernel", "batch": BATCH, "context": ctx_len, "us_per_launch": round(us, 2),
+        line.update({"kernel": "decode_attn_rows_kernel", "batch": BATCH, "context": ctx_len, "us_per_launch": round(us, 2),
                      "algorithmic_bytes": nbytes, "gbs": round(nbytes / us / 1e3, 1)})
     elif name == "rmsnorm_quant":
         x = torch.randn(BATCH, h, device=device, generator=g).half()
