@@ -311,6 +311,10 @@ def test_decode_attention_reference_fixture(K):
     (8, 32, 32, 256, [1024, 1087, 1000, 1, 0, 257, 512, 768]),  # 7B decode, incl. a padded row (ctx 0)
     (3, 8, 2, 16, [5, 70, 33]),
     (2, 4, 4, 64, [300, 64]),
+    (3, 64, 8, 32, [700, 33, 0]),    # 4 heads per consumer warp (16 dims per lane)
+    (2, 48, 16, 16, [300, 64]),      # 12 consumer warps, 8-token stages
+    (2, 6, 2, 16, [90, 200]),        # H not a multiple of 4: the per-head kernel
+    (2, 8, 8, 256, [1, 2]),
 ])
 def test_decode_attention_vs_oracle(K, b, h, hkv, bs, ctx):
     d = 128
