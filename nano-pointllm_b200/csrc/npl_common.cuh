@@ -118,8 +118,8 @@ __device__ __forceinline__ float scale_from_absmax(float absmax) {
 // |v / s| >= 1/2 makes |v| >= 2^-15 and |e| >= ulp(q1 s) / 2 >= 2^-40; for
 // |v / s| < 1/2 the rounded integer is 0 either way (q stays below 1/2 or
 // rounds to it, and rint(+-1/2) = 0). The tests check every finite fp16 v
-// against IEEE division for ~200 scales spread over the fp16 range (the
-// scales are fp16 values), and fp32 v by sampling.
+// against IEEE division at every scale the quantiser can produce (the 23377
+// fp16 values from 2^-14 to 516), exhaustively, and fp32 v by sampling.
 __device__ __forceinline__ float quant_recip(float s) { return __frcp_rn(s); }
 
 __device__ __forceinline__ int quantize_one(float v, float s, float r) {

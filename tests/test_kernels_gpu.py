@@ -78,6 +78,31 @@ def test_quant_rows_every_fp16_value(K):
     np.testing.assert_array_equal(cpu(q), qo)
 
 
+def test_quant_every_fp16_value_at_every_scale(K):
+    """Exhaustive: every finite fp16 value v quantised with every scale the
+    per-token quantiser can produce (every fp16 value s = scale_from_absmax(A)
+    for a finite fp16 absmax A: 23377 scales, 2^-14 .. 516), through npl_quant_rows_absmax:
+    the kernel's quotient (the row's reciprocal + one FMA correction step)
+    rounds like the IEEE fp32 division v / s of the reference, bit for bit,
+    clamp included (|v| beyond 127.5 s)."""
+    allh = np.arange(1 << 16, dtype=np.uint16).view(np.float16)
+    allh = allh[np.isfinite(allh)]  # 63488 values, a multiple of 16
+    amax = np.concatenate([[0.0], allh[allh > 0]]).astype(np.float32)
+    scales = O.scale_from_absmax(amax)
+    _, first = np.unique(scales, return_index=True)
+    amax, scales = amax[first], scales[first]  # one absmax per distinct scale
+    v = torch.from_numpy(allh).to(K.dev)
+    vf = v.float()
+    for c0 in range(0, amax.size, 2048):
+        a = torch.from_numpy(amax[c0:c0 + 2048]).to(K.dev)
+        rows = v.unsqueeze(0).expand(a.numel(), -1).contiguous()
+        q, sc = K.W.quant_rows_absmax(rows, a.view(torch.int32))
+        assert torch.equal(sc, torch.from_numpy(scales[c0:c0 + 2048]).to(K.dev))
+        ref = torch.round(vf.unsqueeze(0) / sc.unsqueeze(1)).clamp(-127, 127).to(torch.int8)
+        assert torch.equal(q, ref), f"scales {c0}..{c0 + a.numel()}"
+    assert amax.size > 23000
+
+
 def test_quant_golden_small(K):
     g = golden("linear_small.npz")
     for tag in ("f32", "f16"):
