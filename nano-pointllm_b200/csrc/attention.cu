@@ -538,8 +538,12 @@ __global__ void __launch_bounds__(kAttnThreads, kAttnCtasPerSm)
 // (and V) row of all kv heads is contiguous (Hkv x 256 bytes; 8 KB at the 7B
 // geometry), and the tokens of a chunk inside one cache block are contiguous
 // too, so every copy is one 1-D bulk copy of several KB. Units are numbered
-// chunk-major (chunk 0 of every sequence, then chunk 1, ...) and dealt out
-// round-robin, so the light last chunks come last.
+// from a prefix sum of the sequences' unit counts (built in shared memory by
+// every CTA, so no number is an empty unit): first every unit but the last of
+// each sequence, sequence by sequence, then the last (partly filled) unit of
+// every sequence, so the light units come last. Each CTA starts with unit
+// blockIdx.x and takes the next ones from a work counter, which keeps the
+// CTAs balanced when the contexts are ragged.
 //
 //   warp 0         producer: for each unit, ring stages of tok_stage tokens
 //                  (K rows then V rows, ~32 KB each) by cp.async.bulk
@@ -584,6 +588,7 @@ struct RowArgs {
   float* part_ml;   // [B][n_chunks][H][2]
   float* part_acc;  // [B][n_chunks][H][128]
   int32_t* cnt;     // [B]: units finished (reset by the unit that merges)
+  int32_t* work;    // [2]: units handed out beyond the first grid.x; CTAs done (reset by the last CTA)
   int* status;
 };
 
@@ -678,6 +683,38 @@ __device__ void rows_finish(const RowArgs& p, float* red, int nthreads, int cw, 
   rows_bar(nthreads);  // red[] is free again
 }
 
+// Merges the partials of sequence b (every unit of it has written its
+// partial) in chunk order and writes out[b]; every consumer thread of the CTA
+// calls it together.
+template <int DPL>
+__device__ void rows_merge(const RowArgs& p, float* red, int nthreads, int cw, int lane, int b, int hq, int j) {
+  using LN = RowLanes<DPL>;
+  const int n_b = max(1, (rows_ctx(p, b) + kRowUnit - 1) / kRowUnit);
+  float mm = kNegBig, ll = 0.f, aa[DPL];
+#pragma unroll
+  for (int i = 0; i < DPL; ++i) aa[i] = 0.f;
+  for (int cidx = 0; cidx < n_b; ++cidx) {
+    const size_t pc = ((size_t)b * p.n_chunks + cidx) * p.H + hq;
+    const float2 ml = __ldcg(reinterpret_cast<const float2*>(p.part_ml) + pc);
+    const float4* src = reinterpret_cast<const float4*>(p.part_acc + pc * 128);
+    float ac[DPL];
+#pragma unroll
+    for (int c = 0; c < LN::CH; ++c) {
+      const float4 x0 = __ldcg(src + 16 * c + 2 * j), x1 = __ldcg(src + 16 * c + 2 * j + 1);
+      ac[8 * c] = x0.x; ac[8 * c + 1] = x0.y; ac[8 * c + 2] = x0.z; ac[8 * c + 3] = x0.w;
+      ac[8 * c + 4] = x1.x; ac[8 * c + 5] = x1.y; ac[8 * c + 6] = x1.z; ac[8 * c + 7] = x1.w;
+    }
+    const float mn = fmaxf(mm, ml.x);
+    const float w0 = exp2f(mm - mn), w1 = exp2f(ml.x - mn);
+    ll = ll * w0 + ml.y * w1;
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) aa[i] = aa[i] * w0 + ac[i] * w1;
+    mm = mn;
+  }
+  if (cw == 0 && lane == 0) p.cnt[b] = 0;  // no other unit of this launch counts b again
+  rows_finish<DPL>(p, red, nthreads, cw, lane, b, hq, j, ll, aa);
+}
+
 template <int DPL>
 __global__ void __launch_bounds__(32 * (kRowMaxWarps + 1), 1) decode_attn_rows_kernel(const RowArgs p) {
   using LN = RowLanes<DPL>;
@@ -691,7 +728,8 @@ __global__ void __launch_bounds__(32 * (kRowMaxWarps + 1), 1) decode_attn_rows_k
   uint64_t* empty = full + p.n_stages;
   int4* meta = reinterpret_cast<int4*>(empty + p.n_stages);
   float* red = reinterpret_cast<float*>(meta + p.n_stages);
-  int* merge_flag = reinterpret_cast<int*>(red + kRowMaxWarps);
+  int* merge_slot = reinterpret_cast<int*>(red + kRowMaxWarps);  // [2]
+  int* unit_start = merge_slot + 4;                                // [B + 1]: first unit of each sequence
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
@@ -704,21 +742,57 @@ __global__ void __launch_bounds__(32 * (kRowMaxWarps + 1), 1) decode_attn_rows_k
   __syncthreads();
   pdl_trigger();
   pdl_wait();
-  const int n_units = p.n_chunks * p.B;
 
   if (warp == 0) {
     // ---------------------------------------------------------- producer
+    // unit_start[b] = units of the sequences before b (a warp scan per 32 sequences)
+    int run = 0;
+    for (int b0 = 0; b0 < p.B; b0 += 32) {
+      const int b = b0 + lane;
+      int x = b < p.B ? max(1, (rows_ctx(p, b) + kRowUnit - 1) / kRowUnit) : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+      }
+      if (b < p.B) unit_start[b + 1] = run + x;
+      run += __shfl_sync(0xffffffffu, x, 31);
+    }
+    __syncwarp();  // the other lanes' entries before lane 0 reads them
     if (lane != 0) return;
+    unit_start[0] = 0;
+    const int n_units = run;
     const uint64_t pol = policy_evict_first();
     int stage = 0;
     uint32_t phase = 0;
     uint32_t used = 0, parity = 0;  // per ring slot: issued at least once; parity of its last phase
     bool ok = true;
-    for (int u = (int)blockIdx.x; u < n_units && ok; u += (int)gridDim.x) {
-      const int chunk = u / p.B, b = u % p.B;
+    // the first unit of each CTA is blockIdx.x; the following ones come from
+    // the work counter (which counts units beyond the first grid.x), when
+    // there are more units than CTAs
+    const bool dynamic = n_units > (int)gridDim.x;
+    int next = (int)blockIdx.x;
+    while (ok) {
+      const int u = next;
+      if (u >= n_units) break;
+      next = dynamic ? (int)gridDim.x + atomicAdd(p.work, 1) : n_units;
+      // units [0, n_units - B): the non-last units, sequence b's starting at
+      // unit_start[b] - b; units [n_units - B, n_units): the last units
+      const int n_inner = n_units - p.B;
+      int b, chunk;
+      if (u < n_inner) {
+        b = 0;  // the last b with unit_start[b] - b <= u
+        for (int hi = p.B - 1; b < hi;) {
+          const int mid = (b + hi + 1) >> 1;
+          if (unit_start[mid] - mid <= u) b = mid;
+          else hi = mid - 1;
+        }
+        chunk = u - (unit_start[b] - b);
+      } else {
+        b = u - n_inner;
+        chunk = unit_start[b + 1] - unit_start[b] - 1;
+      }
       const int ctx = rows_ctx(p, b);
-      const int n_b = max(1, (ctx + kRowUnit - 1) / kRowUnit);
-      if (chunk >= n_b) continue;
       const int t0 = chunk * kRowUnit, t_end = min(ctx, t0 + kRowUnit);
       const int n_st = max(1, (t_end - t0 + p.tok_stage - 1) / p.tok_stage);
       const int32_t* table = p.bt + (size_t)b * p.bt_stride;
@@ -745,7 +819,7 @@ __global__ void __launch_bounds__(32 * (kRowMaxWarps + 1), 1) decode_attn_rows_k
           ok = false;
           break;
         }
-        meta[stage] = make_int4(u, st, valid, st == n_st - 1);
+        meta[stage] = make_int4(chunk * p.B + b, st, valid, st == n_st - 1);
         used |= 1u << stage;
         parity = (parity & ~(1u << stage)) | (phase << stage);
         mbar_arrive_expect_tx(&full[stage], 2u * (uint32_t)valid * (uint32_t)p.row_bytes);
@@ -771,6 +845,12 @@ __global__ void __launch_bounds__(32 * (kRowMaxWarps + 1), 1) decode_attn_rows_k
       parity = (parity & ~(1u << stage)) | (phase << stage);
       mbar_arrive(&full[stage]);
     }
+    // every CTA counts itself done after its last take from the work counter;
+    // the last one resets both words for the next launch
+    if (dynamic && atomicAdd(p.work + 1, 1) + 1 == (int)gridDim.x) {
+      atomicExch(p.work, 0);
+      atomicExch(p.work + 1, 0);
+    }
     // Copies land before the CTA exits: the last phase of every slot that was
     // issued has completed (at once, unless a wait above expired).
     for (int i = 0; i < p.n_stages; ++i)
@@ -790,11 +870,19 @@ __global__ void __launch_bounds__(32 * (kRowMaxWarps + 1), 1) decode_attn_rows_k
   float m = kNegBig, l = 0.f;
   int stage = 0;
   uint32_t phase = 0;
+  // The count at the end of a unit is taken by thread 0 without waiting for
+  // it; its outcome (this unit completes sequence pend_b) is published at the
+  // next unit end, or after the last unit, through merge_slot[slot].
+  int pend_b = -1, slot = 0;
+  bool pend_last = false, done = false;
   while (true) {
     if (!mbar_wait(&full[stage], phase, p.status, NPL_DEV_TIMEOUT_EPILOGUE)) break;
     const volatile int* mv = reinterpret_cast<volatile int*>(&meta[stage]);
     const int4 mt = make_int4(mv[0], mv[1], mv[2], mv[3]);
-    if (mt.x < 0) break;
+    if (mt.x < 0) {
+      done = true;
+      break;
+    }
     const int chunk = mt.x / p.B, b = mt.x % p.B;
     if (mt.y == 0) {
       const unsigned char* qrow = reinterpret_cast<const unsigned char*>(p.q + ((size_t)b * p.H + hq) * 128);
@@ -877,35 +965,21 @@ __global__ void __launch_bounds__(32 * (kRowMaxWarps + 1), 1) decode_attn_rows_k
       __stcg(pa + 16 * c + 2 * j, make_float4(acc[8 * c], acc[8 * c + 1], acc[8 * c + 2], acc[8 * c + 3]));
       __stcg(pa + 16 * c + 2 * j + 1, make_float4(acc[8 * c + 4], acc[8 * c + 5], acc[8 * c + 6], acc[8 * c + 7]));
     }
-    rows_bar(nthreads);  // every partial write of the CTA before the count (cumulative release)
-    if (cw == 0 && lane == 0) *merge_flag = atomic_add_acq_rel(p.cnt + b, 1) + 1 == n_b;
-    rows_bar(nthreads);
-    if (!*merge_flag) continue;
-    // this unit completes sequence b: merge its partials in chunk order
-    float mm = kNegBig, ll = 0.f, aa[DPL];
-#pragma unroll
-    for (int i = 0; i < DPL; ++i) aa[i] = 0.f;
-    for (int cidx = 0; cidx < n_b; ++cidx) {
-      const size_t pc = ((size_t)b * p.n_chunks + cidx) * p.H + hq;
-      const float2 ml = __ldcg(reinterpret_cast<const float2*>(p.part_ml) + pc);
-      const float4* src = reinterpret_cast<const float4*>(p.part_acc + pc * 128);
-      float ac[DPL];
-#pragma unroll
-      for (int c = 0; c < LN::CH; ++c) {
-        const float4 x0 = __ldcg(src + 16 * c + 2 * j), x1 = __ldcg(src + 16 * c + 2 * j + 1);
-        ac[8 * c] = x0.x; ac[8 * c + 1] = x0.y; ac[8 * c + 2] = x0.z; ac[8 * c + 3] = x0.w;
-        ac[8 * c + 4] = x1.x; ac[8 * c + 5] = x1.y; ac[8 * c + 6] = x1.z; ac[8 * c + 7] = x1.w;
-      }
-      const float mn = fmaxf(mm, ml.x);
-      const float w0 = exp2f(mm - mn), w1 = exp2f(ml.x - mn);
-      ll = ll * w0 + ml.y * w1;
-#pragma unroll
-      for (int i = 0; i < DPL; ++i) aa[i] = aa[i] * w0 + ac[i] * w1;
-      mm = mn;
+    if (cw == 0 && lane == 0) merge_slot[slot] = pend_last ? pend_b : -1;
+    rows_bar(nthreads);  // every partial write of the CTA before the count (cumulative release); the slot
+    const int mb = merge_slot[slot];
+    slot ^= 1;  // (two slots: thread 0 may write the next one before a slow thread has read this one)
+    if (cw == 0 && lane == 0) {
+      pend_b = b;
+      pend_last = atomic_add_acq_rel(p.cnt + b, 1) + 1 == n_b;
     }
-    if (cw == 0 && lane == 0) p.cnt[b] = 0;  // no other unit of this launch counts b again
-    rows_finish<DPL>(p, red, nthreads, cw, lane, b, hq, j, ll, aa);
+    if (mb >= 0) rows_merge<DPL>(p, red, nthreads, cw, lane, mb, hq, j);
   }
+  if (!done) return;  // a bounded wait gave up (the status word says so)
+  if (cw == 0 && lane == 0) merge_slot[slot] = pend_last ? pend_b : -1;
+  rows_bar(nthreads);
+  const int mb = merge_slot[slot];
+  if (mb >= 0) rows_merge<DPL>(p, red, nthreads, cw, lane, mb, hq, j);
 }
 
 // fp16 cache [num_blocks * block_size][Hkv][D] as a 3-D tensor map; box =
@@ -1090,14 +1164,16 @@ extern "C" int npl_paged_decode_attention(const void* q, int B, int H, int Hkv, 
     r.part_ml = reinterpret_cast<float*>(ws + lay.ml);
     r.part_acc = reinterpret_cast<float*>(ws + lay.acc);
     r.cnt = reinterpret_cast<int32_t*>(ws + lay.cnt_row);
+    r.work = reinterpret_cast<int32_t*>(ws + lay.work);
     r.status = device_status_ptr();
     const int sms = num_sms();
     const long long units = (long long)r.n_chunks * B;
     const int grid = (int)std::min<long long>(sms > 0 ? sms : 148, units);
     auto kern = rc.warps * 2 == H ? decode_attn_rows_kernel<8> : decode_attn_rows_kernel<16>;
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rc.smem) != cudaSuccess)
+    const size_t smem = rc.smem + (size_t)(B + 1) * sizeof(int);  // + unit_start
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
       return launch_status("npl_paged_decode_attention: smem attribute");
-    return launch_pdl("npl_paged_decode_attention", kern, dim3(grid), dim3(32 * (rc.warps + 1)), rc.smem,
+    return launch_pdl("npl_paged_decode_attention", kern, dim3(grid), dim3(32 * (rc.warps + 1)), smem,
                       static_cast<cudaStream_t>(stream), r);
   }
   const int box_tok = std::min(kAttnTok, block_size);
