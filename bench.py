@@ -637,21 +637,27 @@ def run_kernel_case(args, torch, device) -> dict:
         line.update({"kernel": "w8a8_linear_kernel", "shape": [BATCH, n, k], "us_per_launch": round(us, 2),
                      "algorithmic_bytes": nbytes, "gbs": round(nbytes / us / 1e3, 1)})
     elif name == "attention":
-        ctx_len, mb = CTX + 16, (CTX + 16 + BLOCK_SIZE - 1) // BLOCK_SIZE + 1
-        nb = BATCH * mb
+        # config 3 by default (8 x 1040 tokens); --attn-batch / --attn-ctx LO HI
+        # give serving-like batches with contexts drawn uniformly from [LO, HI]
+        batch = args.attn_batch or BATCH
+        lo, hi = args.attn_ctx or (CTX + 16, CTX + 16)
+        ctx_l = torch.randint(lo, hi + 1, (batch,), generator=torch.Generator().manual_seed(1)).tolist()
+        mb = (max(ctx_l) + BLOCK_SIZE - 1) // BLOCK_SIZE + 1
+        nb = batch * mb
         sets = [(torch.randn(nb, BLOCK_SIZE, shape.kv_heads, shape.head_dim, device=device, generator=g).half(),
                  torch.randn(nb, BLOCK_SIZE, shape.kv_heads, shape.head_dim, device=device, generator=g).half())
                 for _ in range(3)]
-        bt = S.permuted_block_tables(BATCH, mb, nb, seed=1).to(device)
-        q = torch.randn(BATCH, shape.heads, shape.head_dim, device=device, generator=g).half()
-        cl = torch.full((BATCH,), ctx_len, dtype=torch.int32, device=device)
-        q8 = torch.empty(BATCH, shape.heads * shape.head_dim, dtype=torch.int8, device=device)
-        qs = torch.empty(BATCH, dtype=torch.float32, device=device)
+        bt = S.permuted_block_tables(batch, mb, nb, seed=1).to(device)
+        q = torch.randn(batch, shape.heads, shape.head_dim, device=device, generator=g).half()
+        cl = torch.tensor(ctx_l, dtype=torch.int32, device=device)
+        q8 = torch.empty(batch, shape.heads * shape.head_dim, dtype=torch.int8, device=device)
+        qs = torch.empty(batch, dtype=torch.float32, device=device)
         out = torch.empty_like(q)
         us = timed(lambda i: PA.paged_decode_attention(q, sets[i % 3][0], sets[i % 3][1], bt, cl, shape.head_dim ** -0.5,
                                                         1, out=out, quant_out=(q8, qs)), 1)
-        nbytes = op_bytes(shape, "attention", ctx_len)
-        line.update({"kernel": "decode_attn_rows_kernel", "batch": BATCH, "context": ctx_len, "us_per_launch": round(us, 2),
+        nbytes = sum(op_bytes(shape, "attention", n) for n in ctx_l) // BATCH  # op_bytes counts BATCH sequences
+        line.update({"kernel": "decode_attn_rows_kernel", "batch": batch,
+                     "context": ctx_l[0] if lo == hi else [lo, hi], "us_per_launch": round(us, 2),
                      "algorithmic_bytes": nbytes, "gbs": round(nbytes / us / 1e3, 1)})
     elif name == "rmsnorm_quant":
         x = torch.randn(BATCH, h, device=device, generator=g).half()
@@ -919,6 +925,9 @@ def main() -> int:
     ap.add_argument("--serve-max-seqs", type=int, default=64)
     ap.add_argument("--prefill-seqs", type=int, default=8, help="prefill_attention case: sequences")
     ap.add_argument("--prefill-len", type=int, default=560, help="prefill_attention case: tokens per sequence")
+    ap.add_argument("--attn-batch", type=int, default=0, help="attention case: sequences (default 8)")
+    ap.add_argument("--attn-ctx", type=int, nargs=2, metavar=("LO", "HI"),
+                    help="attention case: contexts drawn uniformly from [LO, HI] (default 1040)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

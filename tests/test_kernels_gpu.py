@@ -400,6 +400,48 @@ def test_decode_attention_shared_workspace(K):
     K.lib.device_status()
 
 
+def test_decode_attention_ragged_batch_more_units_than_sms(K):
+    """A ragged batch of 40 sequences has more 64-token units than the GPU
+    has SMs, so the units are handed out by the work counter: the output stays
+    within tolerance of the oracle, the fused int8 rows equal npl_quant_rows
+    on it, each sequence's row equals the row it gets alone in a batch of one
+    (batch invariance, bit for bit), and the workspace counters are zero
+    afterwards."""
+    from nanopointllm_b200 import synthetic as S
+    b, h, hkv, d, bs = 40, 32, 8, 128, 64
+    gen = torch.Generator().manual_seed(23)
+    ctx = torch.randint(2, 1500, (b,), generator=gen).tolist()
+    ctx[:6] = [0, 1, 64, 65, 1500, 128]
+    assert sum(max(1, -(-n // 64)) for n in ctx) > 200
+    mb = -(-max(ctx) // bs) + 1
+    nb = b * mb
+    kc = torch.randn(nb, bs, hkv, d, generator=gen).half()
+    vc = torch.randn(nb, bs, hkv, d, generator=gen).half()
+    q = torch.randn(b, h, d, generator=gen).half()
+    bt = S.permuted_block_tables(b, mb, nb, seed=5)
+    dev = K.dev
+    kcd, vcd, btd = kc.to(dev), vc.to(dev), bt.to(dev)
+    q8 = torch.empty((b, h * d), dtype=torch.int8, device=dev)
+    qs = torch.empty((b,), dtype=torch.float32, device=dev)
+    ctx_d = torch.tensor(ctx, dtype=torch.int32, device=dev)
+    out = K.PA.paged_decode_attention(q.to(dev), kcd, vcd, btd, ctx_d, d ** -0.5, h // hkv, quant_out=(q8, qs))
+    ref = O.paged_decode_attention(q.numpy(), kc.numpy(), vc.numpy(), bt.numpy(), ctx, d ** -0.5, h // hkv)
+    np.testing.assert_allclose(cpu(out).astype(np.float64), ref, atol=2e-3, rtol=2e-3)
+    ref_q, ref_s = K.W.dynamic_per_token_quant(out.reshape(b, -1))
+    torch.cuda.synchronize()
+    assert torch.equal(q8, ref_q) and torch.equal(qs, ref_s.reshape(-1))
+    assert float(out[0].abs().sum()) == 0.0
+    ws = K.PA.decode_attention_workspace(dev, b, h, d, mb, bs)
+    assert int(ws[:256 + 4096 + (4 << 18)].count_nonzero()) == 0
+    for i in (0, 1, 3, 4, 17, 39):
+        alone = K.PA.paged_decode_attention(q[i:i + 1].to(dev), kcd, vcd, btd[i:i + 1].contiguous(),
+                                            ctx_d[i:i + 1].contiguous(), d ** -0.5, h // hkv)
+        assert torch.equal(alone[0], out[i]), f"sequence {i}"
+    out2 = K.PA.paged_decode_attention(q.to(dev), kcd, vcd, btd, ctx_d, d ** -0.5, h // hkv)
+    assert torch.equal(out, out2)
+    K.lib.device_status()
+
+
 def test_decode_attention_fused_quant_equals_quant_rows(K):
     """The per-token int8 quantisation fused into the attention kernel equals
     npl_quant_rows on the attention's own fp16 output, bit for bit (including
