@@ -108,6 +108,16 @@ int npl_dequant_rows(const int8_t* q, int rows, int cols, int ldq, const float* 
                      int ld_out, int out_dtype, void* stream);
 
 /*
+ * act_fn(gate) * up of the unfused MLP on fp16 rows (lightweight_runner.py:358):
+ *   out[r, c] = fp16(fp16(silu(gate[r, c])) * up[r, c])
+ * with SiLU rounded once to fp16 from the exact value, the arithmetic of the
+ * SiLU * up epilogue of npl_w8a8_linear_ex (NPL_EPI_SILU_MUL). cols and the
+ * leading dimensions multiples of 8; pointers 16-byte aligned.
+ */
+int npl_silu_mul(const void* gate, int ld_gate, const void* up, int ld_up, int rows, int cols, void* out, int ld_out,
+                 void* stream);
+
+/*
  * scale_from_absmax (w8a8.py:46-50) over n fp32 absmax values:
  *   scale[i] = max(fp32(fp16(max(absmax[i], fp16.tiny) / 127)), fp16.tiny)
  */

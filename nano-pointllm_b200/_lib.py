@@ -74,6 +74,7 @@ SIGNATURES = {
     "npl_quant_given_scale": (_I, [_P, _I, _I, _I, _I, _P, _I, _P, _I, _P]),
     "npl_dequant_rows": (_I, [_P, _I, _I, _I, _P, _I, _P, _I, _I, _P]),
     "npl_scale_from_absmax": (_I, [_P, _I, _P, _P]),
+    "npl_silu_mul": (_I, [_P, _I, _P, _I, _I, _I, _P, _I, _P]),
     "npl_dequant": (_I, [_P, _I, _P, _P, _P, _I, _I, _I, _P, _I, _P, _I, _I, _P]),
     "npl_rmsnorm_quant": (_I, [_P, _P, _P, _F, _I, _I, _P, _P, _P, _P, _P]),
     "npl_linear_workspace_bytes": (_Z, [_I, _I, _I]),

@@ -234,12 +234,6 @@ __device__ __forceinline__ void load_epi_operands(const LinearArgs& p, int m_til
   }
 }
 
-// silu(g) rounded once to fp16, evaluated in fp64.
-__device__ __forceinline__ float silu_h(float g) {
-  const double gd = (double)g;
-  return __half2float(__double2half(gd / (1.0 + exp(-gd))));
-}
-
 __device__ __forceinline__ void atomic_max_nonneg(int32_t* p, float v) {
   atomicMax(p, __float_as_int(v));  // bit patterns of non-negative floats order like the values
 }
@@ -287,7 +281,7 @@ __device__ __forceinline__ void epilogue_chunk(const LinearArgs& p, LinearCtl& c
         const float other = __half2float(c.xchg[j][gate ? pr : 64 + pr]);
         const float g = gate ? own : other;
         const float u = gate ? other : own;
-        const __half hh = __float2half_rn(__fmul_rn(silu_h(g), u));
+        const __half hh = __float2half_rn(__fmul_rn(silu_f16(g), u));
         out[(size_t)m * p.ld_out + col] = hh;
         h = fabsf(__half2float(hh));
       }
@@ -406,7 +400,7 @@ __device__ __forceinline__ void silu_pair(const LinearArgs& p, LinearCtl& c, con
         const float other = __half2float(c.xchg[j][h ? s_mine : s_other]);
         const float g = gate ? own : other;
         const float u = gate ? other : own;
-        const __half hh = __float2half_rn(__fmul_rn(silu_h(g), u));
+        const __half hh = __float2half_rn(__fmul_rn(silu_f16(g), u));
         out[(size_t)m * p.ld_out + col] = hh;
         a = fabsf(__half2float(hh));
       }

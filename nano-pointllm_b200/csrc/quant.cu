@@ -370,6 +370,44 @@ extern "C" int npl_dequant_rows(const int8_t* q, int rows, int cols, int ldq, co
                     static_cast<cudaStream_t>(stream), q, cols, ldq, scale, scale_stride, out, ld_out, out_dtype);
 }
 
+// act_fn(gate) * up on fp16 rows (lightweight_runner.py:358, the unfused MLP):
+// out = fp16(silu_f16(g) * u), the same arithmetic as the SiLU * up epilogue
+// of npl_w8a8_linear_ex. 8 columns per thread.
+__global__ void __launch_bounds__(256) silu_mul_kernel(const __half* __restrict__ gate, int ld_gate,
+                                                       const __half* __restrict__ up, int ld_up, int cols,
+                                                       __half* __restrict__ out, int ld_out) {
+  pdl_wait();
+  pdl_trigger();
+  const int r = blockIdx.x;
+  const int c0 = (blockIdx.y * 256 + threadIdx.x) * 8;
+  if (c0 >= cols) return;
+  const uint4 g8 = *reinterpret_cast<const uint4*>(gate + (size_t)r * ld_gate + c0);
+  const uint4 u8 = *reinterpret_cast<const uint4*>(up + (size_t)r * ld_up + c0);
+  const __half* g = reinterpret_cast<const __half*>(&g8);
+  const __half* u = reinterpret_cast<const __half*>(&u8);
+  uint4 o8;
+  __half* o = reinterpret_cast<__half*>(&o8);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) o[i] = __float2half_rn(__fmul_rn(silu_f16(__half2float(g[i])), __half2float(u[i])));
+  *reinterpret_cast<uint4*>(out + (size_t)r * ld_out + c0) = o8;
+}
+
+extern "C" int npl_silu_mul(const void* gate, int ld_gate, const void* up, int ld_up, int rows, int cols, void* out,
+                            int ld_out, void* stream) {
+  if (int rc = check_device()) return rc;
+  if (!gate || !up || !out) return fail(NPL_ERR_ARG, "npl_silu_mul: null pointer");
+  if (rows < 0 || cols <= 0 || cols % 8 || ld_gate < cols || ld_gate % 8 || ld_up < cols || ld_up % 8 ||
+      ld_out < cols || ld_out % 8)
+    return fail(NPL_ERR_ARG, "npl_silu_mul: bad shape rows=%d cols=%d ld_gate=%d ld_up=%d ld_out=%d", rows, cols,
+                ld_gate, ld_up, ld_out);
+  if (!aligned16(gate) || !aligned16(up) || !aligned16(out))
+    return fail(NPL_ERR_ARG, "npl_silu_mul: pointers must be 16-byte aligned");
+  if (rows == 0) return NPL_OK;
+  return launch_pdl("npl_silu_mul", silu_mul_kernel, dim3(rows, (cols + 2047) / 2048), dim3(256), 0,
+                    static_cast<cudaStream_t>(stream), static_cast<const __half*>(gate), ld_gate,
+                    static_cast<const __half*>(up), ld_up, cols, static_cast<__half*>(out), ld_out);
+}
+
 extern "C" int npl_scale_from_absmax(const float* absmax, int n, float* scale, void* stream) {
   if (int rc = check_device()) return rc;
   if (!absmax || !scale || n < 0) return fail(NPL_ERR_ARG, "npl_scale_from_absmax: bad arguments");

@@ -386,6 +386,24 @@ def integer_linear_per_output_reference(values: torch.Tensor, weight: torch.Tens
     return _integer_linear(qa, sa, weight, bias, values.shape[:-1])
 
 
+def silu_mul(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    """``act_fn(gate) * up`` of the unfused MLP on fp16 values
+    (lightweight_runner.py:358): fp16(fp16(silu(gate)) * up), SiLU rounded
+    once to fp16 from the exact value (npl_silu_mul, the arithmetic of the
+    SiLU * up epilogue)."""
+    _require_cuda(gate, up)
+    if gate.shape != up.shape or gate.dtype != torch.float16 or up.dtype != torch.float16:
+        raise ValueError("silu_mul: gate and up must be fp16 tensors of one shape")
+    cols = gate.shape[-1] if gate.dim() else 1
+    g = _pad_cols(gate.reshape(-1, cols), 8)
+    u = _pad_cols(up.reshape(-1, cols), 8)
+    out = torch.empty_like(g)
+    if g.shape[0]:
+        L.check(L.lib.npl_silu_mul(g.data_ptr(), g.stride(0), u.data_ptr(), u.stride(0), g.shape[0], g.shape[1],
+                                   out.data_ptr(), out.stride(0), L.stream_ptr(gate.device)))
+    return out[:, :cols].reshape(gate.shape)
+
+
 def pack_gate_up(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
     """Row layout the SiLU*up epilogue reads: per 128-row tile t, gate rows
     [64t, 64t+64) followed by up rows [64t, 64t+64). Works on weights [I, K]
