@@ -61,7 +61,11 @@ namespace {
 
 constexpr int kTileN = 128;   // weight rows per tile (MMA M)
 constexpr int kBlockK = 128;  // K bytes per stage (one 128-byte swizzle atom)
-constexpr int kThreads = 192;
+// Epilogue warpgroups: prefill tiles (NT >= 128) take two, each draining half
+// of the tile's token columns (the epilogue of a 256-token tile is longer than
+// its main loop with one); decode tiles take one.
+__host__ __device__ constexpr int epi_groups_for(int nt) { return nt >= 128 ? 2 : 1; }
+__host__ __device__ constexpr int threads_for(int nt) { return 64 + 128 * epi_groups_for(nt); }
 constexpr int kMaxStages = 12;
 constexpr int kMaxAccBufs = 4;
 constexpr int kCoresidentSmem = 110 * 1024;  // two CTAs per SM (programmatic dependent launch)
@@ -103,6 +107,9 @@ struct LinearArgs {
   int clusters;   // cluster split-K: number of clusters (tile stride)
   int tiles;      // m_tiles * n_tiles
   int red_bufs;   // cluster split-K: partial-tile buffers (1 or 2)
+  int dp_tiles;   // stream-K: tiles [0, dp_tiles) run whole, CTA b taking b, b + grid, ...
+  int raster_g;   // token tiles per raster group (tile numbering, see tile_coords)
+  long long sk_units;  // stream-K units after the whole tiles: (tiles - dp_tiles) * k_blocks
   int stages;
   int x_slots;
   uint32_t off_a, off_b, off_x, off_f, off_r;
@@ -125,7 +132,7 @@ struct LinearCtl {
   uint64_t rfree[2];  // cluster contributor: leader consumed buffer b
   uint32_t tmem_base;
   int last_flag;
-  __half xchg[8][kTileN];  // epilogue exchange between TMEM lanes
+  __half xchg[2][8][kTileN];  // epilogue exchange between TMEM lanes, per warpgroup
 };
 
 // TMEM accumulator ring depth: decode tiles keep 4 accumulators so that the
@@ -139,7 +146,44 @@ __host__ __device__ constexpr uint32_t tmem_cols_for(int nt) {
   return c;
 }
 
-__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// Epilogue warpgroup of this thread (warps 2-5: 0, warps 6-9: 1) and its
+// named barrier; epi_all_bar() joins every epilogue warp of the CTA.
+template <int NT>
+__device__ __forceinline__ int epi_group() {
+  if constexpr (epi_groups_for(NT) == 1) return 0;
+  return (int)(threadIdx.x - 64) >> 7;
+}
+template <int NT>
+__device__ __forceinline__ void epi_bar() {
+  if constexpr (epi_groups_for(NT) == 1)
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+  else
+    asm volatile("bar.sync %0, 128;" ::"r"(1 + epi_group<NT>()) : "memory");
+}
+__device__ __forceinline__ void epi_all_bar(int groups) {
+  asm volatile("bar.sync 3, %0;" ::"r"(128 * groups) : "memory");
+}
+
+// Tile t of the numbering -> (token tile m, weight tile n). Tiles go in groups
+// of raster_g token tiles: inside a group the token tile runs fastest, so the
+// CTAs working on consecutive tiles at one time share raster_g token tiles and
+// about grid / raster_g weight tiles, which L2 then serves to all of them.
+// raster_g = 1 is the plain order (weight tile fastest).
+template <int NT>
+__device__ __forceinline__ void tile_coords(const LinearArgs& p, int t, int& m, int& n) {
+  if constexpr (NT <= 64) {  // decode tiles: one raster group (weight tile fastest)
+    m = t / p.n_tiles;
+    n = t - m * p.n_tiles;
+    return;
+  }
+  const int g = p.raster_g;
+  const int span = g * p.n_tiles;
+  const int grp = t / span, r = t - grp * span;
+  const int m0 = grp * g;
+  const int gs = min(g, p.tiles / p.n_tiles - m0);
+  m = m0 + r % gs;
+  n = r / gs;
+}
 
 __device__ __forceinline__ int atomic_add_acq_rel(int32_t* p, int v) {
   int old;
@@ -161,14 +205,18 @@ struct SplitRange {
 };
 
 // Iterates the CTA's segments (tile, kb0, kb1).
-//   stream-K (split == 0): the CTA's contiguous share of the (tile, k-block)
-//     units, cut at tile boundaries;
+//   stream-K (split == 0): first the whole tiles blockIdx.x, + grid, ... below
+//     dp_tiles, then the CTA's contiguous share of the remaining (tile,
+//     k-block) units, cut at tile boundaries;
 //   cluster split-K: tiles cluster, cluster + clusters, ... with the k-block
 //     range of the CTA's rank.
+template <int NT>
 struct SegmentIter {
+  static constexpr bool kWholeTiles = NT >= 128;  // decode tiles run no data-parallel phase
   long long u, u1;
   int k_blocks;
   int tile_next, tile_step, tiles, lo, hi;
+  int dp_next, dp_tiles;
   bool split;
   __device__ explicit SegmentIter(const LinearArgs& p) {
     k_blocks = p.k_blocks;
@@ -181,10 +229,14 @@ struct SegmentIter {
       lo = r.lo;
       hi = r.hi;
       u = u1 = 0;
+      dp_next = dp_tiles = 0;
     } else {
-      u = (long long)blockIdx.x * p.total_units / gridDim.x;
-      u1 = (long long)(blockIdx.x + 1) * p.total_units / gridDim.x;
+      const long long base = (long long)p.dp_tiles * k_blocks;
+      u = base + (long long)blockIdx.x * p.sk_units / gridDim.x;
+      u1 = base + (long long)(blockIdx.x + 1) * p.sk_units / gridDim.x;
       tile_next = tile_step = tiles = lo = hi = 0;
+      dp_next = (int)blockIdx.x;
+      dp_tiles = p.dp_tiles;
     }
   }
   __device__ bool next(int& tile, int& kb0, int& kb1) {
@@ -194,6 +246,13 @@ struct SegmentIter {
       tile_next += tile_step;
       kb0 = lo;
       kb1 = hi;
+      return true;
+    }
+    if (kWholeTiles && dp_next < dp_tiles) {
+      tile = dp_next;
+      dp_next += (int)gridDim.x;
+      kb0 = 0;
+      kb1 = k_blocks;
       return true;
     }
     if (u >= u1) return false;
@@ -216,19 +275,21 @@ __device__ __forceinline__ float dequant(int32_t acc, float sa, float sw, const 
 // weight scale and bias of the row, and the residual of the first 8 tokens.
 struct EpiOperands {
   float sw, bias;
+  int c_first;  // first token column of the residuals below
   __half res[8];
 };
 
 template <int NT>
-__device__ __forceinline__ void load_epi_operands(const LinearArgs& p, int m_tile, int n_tile, int row,
+__device__ __forceinline__ void load_epi_operands(const LinearArgs& p, int m_tile, int n_tile, int row, int c_first,
                                                   EpiOperands& e) {
   const int n = n_tile * kTileN + row;
   e.sw = n < p.N ? p.sw[n] : 0.f;
   e.bias = (p.bias && n < p.N) ? p.bias[n] : 0.f;
+  e.c_first = c_first;
   if (p.epilogue == NPL_EPI_RESIDUAL) {
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      const int m = m_tile * NT + j;
+      const int m = m_tile * NT + c_first + j;
       e.res[j] = (m < p.M && n < p.N) ? p.residual[(size_t)m * p.ld_res + n] : __float2half_rn(0.f);
     }
   }
@@ -247,6 +308,7 @@ __device__ __forceinline__ void epilogue_chunk(const LinearArgs& p, LinearCtl& c
   const int n = n_tile * kTileN + row;
   const int m_base = m_tile * NT + c0;
   const int lane = threadIdx.x & 31;
+  const int eg = epi_group<NT>();
   if (p.acc_out && n < p.N) {
 #pragma unroll
     for (int j = 0; j < 8; ++j)
@@ -265,10 +327,10 @@ __device__ __forceinline__ void epilogue_chunk(const LinearArgs& p, LinearCtl& c
     for (int j = 0; j < 8; ++j) {
       if (gate == (j >= 4)) {
         const int m = min(m_base + j, p.M - 1);
-        c.xchg[j][gate ? 64 + pr : pr] = __float2half_rn(dequant(acc[j], sa[m], sw, p.bias, e.bias));
+        c.xchg[eg][j][gate ? 64 + pr : pr] = __float2half_rn(dequant(acc[j], sa[m], sw, p.bias, e.bias));
       }
     }
-    epi_bar();
+    epi_bar<NT>();
     const int col = n_tile * 64 + pr;
     __half* out = static_cast<__half*>(p.out);
 #pragma unroll
@@ -278,7 +340,7 @@ __device__ __forceinline__ void epilogue_chunk(const LinearArgs& p, LinearCtl& c
       float h = 0.f;
       if (m < p.M) {
         const float own = __half2float(__float2half_rn(dequant(acc[j], sa[m], sw, p.bias, e.bias)));
-        const float other = __half2float(c.xchg[j][gate ? pr : 64 + pr]);
+        const float other = __half2float(c.xchg[eg][j][gate ? pr : 64 + pr]);
         const float g = gate ? own : other;
         const float u = gate ? other : own;
         const __half hh = __float2half_rn(__fmul_rn(silu_f16(g), u));
@@ -290,7 +352,7 @@ __device__ __forceinline__ void epilogue_chunk(const LinearArgs& p, LinearCtl& c
         if (lane == 0 && m < p.M) atomic_max_nonneg(p.absmax_out + m, h);
       }
     }
-    epi_bar();
+    epi_bar<NT>();
     return;
   }
   if (p.epilogue == NPL_EPI_ROPE_KV) {
@@ -300,16 +362,16 @@ __device__ __forceinline__ void epilogue_chunk(const LinearArgs& p, LinearCtl& c
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const int m = min(m_base + j, p.M - 1);
-      c.xchg[j][row] = __float2half_rn(dequant(acc[j], sa[m], sw, p.bias, e.bias));
+      c.xchg[eg][j][row] = __float2half_rn(dequant(acc[j], sa[m], sw, p.bias, e.bias));
     }
-    epi_bar();
+    epi_bar<NT>();
     const int q_cols = p.heads * D, k_cols = p.kv_heads * D;
     const int d = n % D;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const int m = m_base + j;
       if (m >= p.M) break;
-      const __half x = c.xchg[j][row];
+      const __half x = c.xchg[eg][j][row];
       const long long slot = p.slots[m];
       const bool slot_ok = slot >= 0 && slot < p.num_slots;
       if (n >= q_cols + k_cols) {  // v
@@ -319,7 +381,7 @@ __device__ __forceinline__ void epilogue_chunk(const LinearArgs& p, LinearCtl& c
       const long long pos = p.positions[m];
       if (pos < 0 || pos >= p.max_position) continue;
       const float x1 = __half2float(x);
-      const float x2 = __half2float(c.xchg[j][row ^ half_d]);
+      const float x2 = __half2float(c.xchg[eg][j][row ^ half_d]);
       const float cs = __half2float(p.cos_t[pos * D + d]);
       const float sn = __half2float(p.sin_t[pos * D + d]);
       // rotate_half(x)[d] = -x[d + D/2] (d < D/2), x[d - D/2] (d >= D/2)
@@ -331,7 +393,7 @@ __device__ __forceinline__ void epilogue_chunk(const LinearArgs& p, LinearCtl& c
       else if (slot_ok)
         p.k_cache[(slot * p.kv_heads + (n - q_cols) / D) * D + d] = o;
     }
-    epi_bar();
+    epi_bar<NT>();
     return;
   }
   if (n >= p.N) return;
@@ -343,7 +405,7 @@ __device__ __forceinline__ void epilogue_chunk(const LinearArgs& p, LinearCtl& c
     const float v = dequant(acc[j], sa[m], sw, p.bias, e.bias);
     if (p.epilogue == NPL_EPI_RESIDUAL) {
       const float o = __half2float(__float2half_rn(v));
-      const float r = __half2float(c0 == 0 ? e.res[j] : p.residual[(size_t)m * p.ld_res + n]);
+      const float r = __half2float(c0 == e.c_first ? e.res[j] : p.residual[(size_t)m * p.ld_res + n]);
       static_cast<__half*>(p.out)[(size_t)m * p.ld_out + n] = __float2half_rn(__fadd_rn(o, r));
     } else if (p.out_dtype == NPL_F32) {
       static_cast<float*>(p.out)[(size_t)m * p.ld_out + n] = v;
@@ -365,6 +427,7 @@ __device__ __forceinline__ void silu_pair(const LinearArgs& p, LinearCtl& c, con
   const int n = n_tile * kTileN + row;
   const int m_base = m_tile * NT + c0;
   const int lane = threadIdx.x & 31;
+  const int eg = epi_group<NT>();
   if (p.acc_out && n < p.N) {
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
@@ -381,11 +444,11 @@ __device__ __forceinline__ void silu_pair(const LinearArgs& p, LinearCtl& c, con
   for (int j = 0; j < 8; ++j) {
     if (gate == (j >= 4)) {
       const int m0 = min(m_base + j, p.M - 1), m1 = min(m_base + 8 + j, p.M - 1);
-      c.xchg[j][s_mine] = __float2half_rn(dequant(a0[j], sa[m0], sw, p.bias, e.bias));
-      c.xchg[j][s_other] = __float2half_rn(dequant(a1[j], sa[m1], sw, p.bias, e.bias));
+      c.xchg[eg][j][s_mine] = __float2half_rn(dequant(a0[j], sa[m0], sw, p.bias, e.bias));
+      c.xchg[eg][j][s_other] = __float2half_rn(dequant(a1[j], sa[m1], sw, p.bias, e.bias));
     }
   }
-  epi_bar();
+  epi_bar<NT>();
   const int col = n_tile * 64 + pr;
   __half* out = static_cast<__half*>(p.out);
 #pragma unroll
@@ -397,7 +460,7 @@ __device__ __forceinline__ void silu_pair(const LinearArgs& p, LinearCtl& c, con
       float a = 0.f;
       if (m < p.M) {
         const float own = __half2float(__float2half_rn(dequant(h ? a1[j] : a0[j], sa[m], sw, p.bias, e.bias)));
-        const float other = __half2float(c.xchg[j][h ? s_mine : s_other]);
+        const float other = __half2float(c.xchg[eg][j][h ? s_mine : s_other]);
         const float g = gate ? own : other;
         const float u = gate ? other : own;
         const __half hh = __float2half_rn(__fmul_rn(silu_f16(g), u));
@@ -410,7 +473,7 @@ __device__ __forceinline__ void silu_pair(const LinearArgs& p, LinearCtl& c, con
       }
     }
   }
-  epi_bar();
+  epi_bar<NT>();
 }
 
 // Residual epilogue of 8 token columns [c0, c0 + 8) of tile row `row`, with
@@ -445,8 +508,11 @@ __device__ __forceinline__ void residual_chunk(const LinearArgs& p, const float*
 template <int NT, typename AccFn>
 __device__ __forceinline__ void epilogue_tile(const LinearArgs& p, LinearCtl& c, const float* sa, int m_tile,
                                               int n_tile, int row, const EpiOperands& e, AccFn&& get_acc) {
+  // this warpgroup's token columns [cb, ce)
+  constexpr int kCols = NT / epi_groups_for(NT);
+  const int cb = e.c_first, ce = cb + kCols;
   if (NT >= 16 && p.epilogue == NPL_EPI_SILU_MUL) {
-    for (int c0 = 0; c0 < NT; c0 += 16) {
+    for (int c0 = cb; c0 < ce; c0 += 16) {
       int32_t a0[8], a1[8];
       get_acc(c0, a0);
       get_acc(c0 + 8, a1);
@@ -455,20 +521,20 @@ __device__ __forceinline__ void epilogue_tile(const LinearArgs& p, LinearCtl& c,
     return;
   }
   if (p.epilogue != NPL_EPI_RESIDUAL) {
-    for (int c0 = 0; c0 < NT; c0 += 8) {
+    for (int c0 = cb; c0 < ce; c0 += 8) {
       int32_t acc[8];
       get_acc(c0, acc);
       epilogue_chunk<NT>(p, c, sa, m_tile, n_tile, row, c0, acc, e);
     }
     return;
   }
-  constexpr int G = NT < 32 ? NT : 32;
+  constexpr int G = kCols < 32 ? kCols : 32;
   const int n = n_tile * kTileN + row;
-  for (int g0 = 0; g0 < NT; g0 += G) {
+  for (int g0 = cb; g0 < ce; g0 += G) {
     __half res[G];
 #pragma unroll
     for (int j = 0; j < G; ++j) {
-      if (g0 == 0 && j < 8) {
+      if (g0 == cb && j < 8) {
         res[j] = e.res[j];
       } else {
         const int m = m_tile * NT + g0 + j;
@@ -541,7 +607,7 @@ __device__ void produce_activations(const LinearArgs& p, int8_t* xslot, float* s
         ss[r] = warp_sum(ss[r]);
         if (lane == 0) red[ew * kRowGroup + r] = ss[r];
       }
-      epi_bar();
+      epi_bar<NT>();
       float rr[kRowGroup];
 #pragma unroll
       for (int r = 0; r < kRowGroup; ++r) {
@@ -550,7 +616,7 @@ __device__ void produce_activations(const LinearArgs& p, int8_t* xslot, float* s
         rr[r] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
         amax[r] = 0.f;
       }
-      epi_bar();  // red is reused below
+      epi_bar<NT>();  // red is reused below
       // pass 2 (L1-resident rows): absmax of the normalised row
       for (int k0 = 0; k0 < p.K; k0 += 128 * 8 * kRowChunks) {
         uint4 buf[kRowGroup][kRowChunks], wbuf[kRowChunks];
@@ -585,7 +651,7 @@ __device__ void produce_activations(const LinearArgs& p, int8_t* xslot, float* s
         const float a = warp_max(amax[r]);
         if (lane == 0) red[ew * kRowGroup + r] = (double)a;
       }
-      epi_bar();
+      epi_bar<NT>();
       if (ct < kRowGroup && m0 + ct < p.M) {
         const float a = fmaxf(fmaxf((float)red[ct], (float)red[kRowGroup + ct]),
                               fmaxf((float)red[2 * kRowGroup + ct], (float)red[3 * kRowGroup + ct]));
@@ -593,14 +659,14 @@ __device__ void produce_activations(const LinearArgs& p, int8_t* xslot, float* s
         s_scale[m0 + ct] = scale_from_absmax(a);
         s_recip[m0 + ct] = quant_recip(s_scale[m0 + ct]);
       }
-      epi_bar();
+      epi_bar<NT>();
     }
   } else {
     for (int m = ct; m < p.M; m += 128) {
       s_scale[m] = scale_from_absmax(__int_as_float(p.x_absmax[m]));
       s_recip[m] = quant_recip(s_scale[m]);
     }
-    epi_bar();
+    epi_bar<NT>();
   }
   // Token tile slots: stream-K keeps one per unit of the CTA (slot u holds
   // k-block (u_begin + u) % k_blocks); cluster split-K one per k-block of the
@@ -670,7 +736,7 @@ __device__ void produce_activations(const LinearArgs& p, int8_t* xslot, float* s
 // kXF16: the fp16-activation modes (their prologue costs registers, so the
 // int8-activation kernel is compiled without it).
 template <int NT, bool kXF16>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(threads_for(NT), 1)
     w8a8_linear_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                        const LinearArgs p) {
   extern __shared__ unsigned char smem_raw[];
@@ -687,6 +753,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int kAccBufs = acc_bufs_for(NT);
   constexpr uint32_t kIdesc = idesc_i8(kTileN, NT);
   constexpr bool x_int8 = !kXF16;
+  constexpr int kEpiGroups = epi_groups_for(NT);
+  static_assert(kEpiGroups == 1 || !kXF16, "the fp16-activation prologue runs on one epilogue warpgroup");
   const uint32_t stage_bytes = kTileN * kBlockK + (x_int8 ? NT * kBlockK : 0);
   const int stages = p.stages;
 
@@ -702,7 +770,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < kAccBufs; ++i) {
       mbar_init(&c.tfull[i], 1);
-      mbar_init(&c.tempty[i], 4);
+      mbar_init(&c.tempty[i], 4 * kEpiGroups);
     }
     mbar_init(&c.teardown, 1);
     mbar_init(&c.xready, 128);
@@ -717,7 +785,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (clustered) {
     // the leader's partial-tile buffers start at zero: contributors add into
     // them through the async proxy
-    for (int i = threadIdx.x; i < p.red_bufs * NT * kTileN; i += kThreads) red[i] = 0;
+    for (int i = threadIdx.x; i < p.red_bufs * NT * kTileN; i += (int)blockDim.x) red[i] = 0;
     fence_proxy_async_smem();
   }
   if (warp == 1) {
@@ -750,10 +818,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       // delay the previous kernel's completion and this kernel's token loads.)
       int pre = 0;
       {
-        SegmentIter it(p);
+        SegmentIter<NT> it(p);
         int tile, kb0, kb1;
         while (pre < stages && it.next(tile, kb0, kb1)) {
-          const int n_tile = tile % p.n_tiles;
+          int m_tile, n_tile;
+          tile_coords<NT>(p, tile, m_tile, n_tile);
           for (int kb = kb0; kb < kb1 && pre < stages; ++kb, ++pre) {
             mbar_arrive_expect_tx(&c.full[pre], stage_bytes);
             tma_load_2d(ring_a + (size_t)pre * kTileN * kBlockK, &tmap_w, kb * kBlockK, n_tile * kTileN,
@@ -764,12 +833,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t outstanding = (1u << pre) - 1;  // stages holding a load (pre <= 12)
       if (clustered) cluster_wait_acquire();
       pdl_wait();
-      SegmentIter it(p);
+      SegmentIter<NT> it(p);
       int tile, kb0, kb1, stage = 0, unit = 0;
       uint32_t phase = 0;
       bool ok = true;
       while (ok && it.next(tile, kb0, kb1)) {
-        const int m_tile = tile / p.n_tiles, n_tile = tile % p.n_tiles;
+        int m_tile, n_tile;
+        tile_coords<NT>(p, tile, m_tile, n_tile);
         for (int kb = kb0; kb < kb1; ++kb, ++unit) {
           if (unit >= pre) {
             if (!mbar_wait(&c.empty[stage], phase ^ 1, p.status, NPL_DEV_TIMEOUT_TMA)) {
@@ -802,7 +872,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       bool ok = x_int8 || mbar_wait(&c.xready, 0, p.status, NPL_DEV_TIMEOUT_MMA);
-      SegmentIter it(p);
+      SegmentIter<NT> it(p);
       int tile, kb0, kb1, stage = 0, seg = 0, unit = 0;
       uint32_t phase = 0;
       while (ok && it.next(tile, kb0, kb1)) {
@@ -844,7 +914,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // -------------------------------------------------------------- epilogue
     const int quarter = warp & 3;  // TMEM lanes this warp may access
     const int row = quarter * 32 + lane;
-    const int ct = threadIdx.x - 64;
+    const int ct = threadIdx.x - 64;  // 0 .. 128 * kEpiGroups - 1
+    const int c_first = epi_group<NT>() * (NT / kEpiGroups);  // this warpgroup's first token column
     pdl_wait();
     if constexpr (kXF16) {
       produce_activations<NT>(p, xslot, s_scale, s_inv, s_recip, reinterpret_cast<double*>(s_recip + NT), ct);
@@ -852,7 +923,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (p.x_mode == NPL_X_F16_ABSMAX) {
         // x_absmax is consumed: the last CTA to have read it zeroes it for the
         // producer of the next call
-        epi_bar();
+        epi_bar<NT>();
         if (ct == 0 && atomic_add_acq_rel(p.ws_xcnt, 1) + 1 == (int)gridDim.x) {
           for (int m = 0; m < p.M; ++m) p.x_absmax[m] = 0;
           *p.ws_xcnt = 0;
@@ -864,8 +935,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float* sa = s_scale;
     if (x_int8) {
       if (p.M <= NT) {
-        for (int m = ct; m < p.M; m += 128) s_scale[m] = p.sa[m];
-        epi_bar();
+        for (int m = ct; m < p.M; m += 128 * kEpiGroups) s_scale[m] = p.sa[m];
+        epi_all_bar(kEpiGroups);
       } else {
         sa = p.sa;
       }
@@ -882,15 +953,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t red_bytes = (uint32_t)(NT * kTileN * sizeof(int32_t));
     const int cluster_tiles =
         clustered ? (p.tiles - (int)(blockIdx.x / (unsigned)p.split) + p.clusters - 1) / p.clusters : 0;
-    SegmentIter it(p);
+    SegmentIter<NT> it(p);
     int tile, kb0, kb1, seg = 0;
     while (it.next(tile, kb0, kb1)) {
       const int buf = seg % kAccBufs;
       const uint32_t tphase = (seg / kAccBufs) & 1;
-      const int m_tile = tile / p.n_tiles, n_tile = tile % p.n_tiles;
+      int m_tile, n_tile;
+      tile_coords<NT>(p, tile, m_tile, n_tile);
       const bool contributor = clustered && !leader;
       EpiOperands eo;
-      if (!contributor) load_epi_operands<NT>(p, m_tile, n_tile, row, eo);
+      if (!contributor) load_epi_operands<NT>(p, m_tile, n_tile, row, c_first, eo);
       if (!mbar_wait(&c.tfull[buf], tphase, p.status, NPL_DEV_TIMEOUT_EPILOGUE)) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(buf * NT);
@@ -915,7 +987,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (lane == 0) mbar_arrive(&c.tempty[buf]);
           if (seg + p.red_bufs < cluster_tiles) {
             fence_proxy_async_smem();  // the cleared cells, before the contributors' next adds
-            epi_bar();
+            epi_bar<NT>();
             if (ct > 0 && ct < p.split) mbar_arrive_remote(cluster_map(&c.rfree[rb], (uint32_t)ct));
           }
         } else {
@@ -938,9 +1010,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         continue;
       }
       const bool whole = (kb0 == 0 && kb1 == p.k_blocks);
-      // slot = (first CTA boundary strictly inside the tile) - 1
-      const long long first_unit = (long long)tile * p.k_blocks;
-      const int slot = (int)(((first_unit + 1) * gridDim.x + p.total_units - 1) / p.total_units) - 1;
+      // a partial tile lies in the stream-K range: slot = (first CTA boundary
+      // strictly inside the tile, counted in that range's units) - 1
+      int slot = 0;
+      if (!whole) {
+        const long long first_unit = (long long)(tile - p.dp_tiles) * p.k_blocks;
+        slot = (int)(((first_unit + 1) * gridDim.x + p.sk_units - 1) / p.sk_units) - 1;
+      }
       int32_t* ws = p.ws_acc + (size_t)slot * NT * kTileN;
       if (whole) {
         epilogue_tile<NT>(p, c, sa, m_tile, n_tile, row, eo, [&](int c0, int32_t(&acc)[8]) {
@@ -948,7 +1024,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_wait_ld();
         });
       } else {
-        for (int c0 = 0; c0 < NT; c0 += 8) {
+        for (int c0 = c_first; c0 < c_first + NT / kEpiGroups; c0 += 8) {
           int32_t acc[8];
           tmem_ld_x8(taddr + c0, acc);
           tmem_wait_ld();
@@ -962,9 +1038,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&c.tempty[buf]);
       if (!whole) {
-        epi_bar();
+        epi_all_bar(kEpiGroups);  // every warpgroup's adds before the count
         if (ct == 0) c.last_flag = (atomic_add_acq_rel(p.ws_cnt + slot, kb1 - kb0) + (kb1 - kb0) == p.k_blocks);
-        epi_bar();
+        epi_all_bar(kEpiGroups);
         if (c.last_flag) {
           epilogue_tile<NT>(p, c, sa, m_tile, n_tile, row, eo, [&](int c0, int32_t(&acc)[8]) {
 #pragma unroll
@@ -976,7 +1052,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           });
           if (ct == 0) p.ws_cnt[slot] = 0;
         }
-        epi_bar();
+        epi_all_bar(kEpiGroups);  // last_flag is read before the next tile sets it
       }
       ++seg;
     }
@@ -1052,7 +1128,7 @@ constexpr uint32_t align1k(size_t x) { return (uint32_t)((x + 1023) & ~size_t(10
 
 // Clusters of `split` CTAs of `kern` with `smem` bytes that fit on the
 // device at once (cached per device, kernel, shared memory and size).
-int max_active_clusters(const void* kern, int smem, int split) {
+int max_active_clusters(const void* kern, int smem, int split, int block) {
   struct Entry {
     int dev;
     const void* kern;
@@ -1067,7 +1143,7 @@ int max_active_clusters(const void* kern, int smem, int split) {
     if (e.dev == dev && e.kern == kern && e.smem == smem && e.split == split) return e.n;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)split);
-  cfg.blockDim = dim3(kThreads);
+  cfg.blockDim = dim3(block);
   cfg.dynamicSmemBytes = (size_t)smem;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -1103,11 +1179,11 @@ struct Schedule {
 // (measured on B200: ~1 us against 0.35 us per 16 KB weight unit).
 constexpr int kStreamKFixupUnits = 3;
 
-Schedule pick_schedule(const void* kern, int tiles, int k_blocks, long long units, int grid_max) {
+Schedule pick_schedule(const void* kern, int block, int tiles, int k_blocks, long long units, int grid_max) {
   Schedule best{0, 0};
   long long best_cost = (units + grid_max - 1) / grid_max + kStreamKFixupUnits;
   for (int s = 1; s <= 8 && s <= k_blocks; ++s) {
-    const int cap = s == 1 ? grid_max : max_active_clusters(kern, kOnePerSmSmem, s);
+    const int cap = s == 1 ? grid_max : max_active_clusters(kern, kOnePerSmSmem, s, block);
     const int c = std::min(tiles, std::min(cap, grid_max / s));
     if (c < 1) continue;
     const long long cost = (long long)((tiles + c - 1) / c) * ((k_blocks + s - 1) / s);
@@ -1147,17 +1223,31 @@ int layout_linear(LinearArgs& p) {
   return (int)(p.off_f + tail + 1024);
 }
 
+// Token tiles per raster group of the prefill tile numbering (tile_coords):
+// the ~148 tiles in flight then share 8 token tiles (8 x 256 rows of
+// activations) and ~18 weight tiles, read from DRAM once per wave.
+constexpr int kRasterGroup = 8;
+
 template <int NT>
 int launch_linear(const CUtensorMap& tw, const CUtensorMap& tx, LinearArgs& p, cudaStream_t st) {
   const bool x_int8 = p.x_mode == NPL_X_INT8;
-  auto kern = x_int8 ? w8a8_linear_kernel<NT, false> : w8a8_linear_kernel<NT, true>;
+  void (*kern)(CUtensorMap, CUtensorMap, LinearArgs);
+  if constexpr (NT > 64) {
+    if (!x_int8) return fail(NPL_ERR_UNSUPPORTED, "npl_w8a8_linear: fp16 activations take at most 64 tokens");
+    kern = w8a8_linear_kernel<NT, false>;
+  } else {
+    kern = x_int8 ? w8a8_linear_kernel<NT, false> : w8a8_linear_kernel<NT, true>;
+  }
+  p.raster_g = 1;
+  p.dp_tiles = 0;
+  p.sk_units = p.total_units;
   const int grid_max = max_grid();
   const void* kfn = reinterpret_cast<const void*>(kern);
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem) != cudaSuccess)
     return launch_status("npl_w8a8_linear: smem attribute");
   int smem = 0, grid = 0;
   if (NT <= 64) {
-    const Schedule s = pick_schedule(kfn, p.tiles, p.k_blocks, p.total_units, grid_max);
+    const Schedule s = pick_schedule(kfn, threads_for(NT), p.tiles, p.k_blocks, p.total_units, grid_max);
     if (s.split > 0) {
       p.split = s.split;
       p.clusters = s.clusters;
@@ -1165,20 +1255,29 @@ int launch_linear(const CUtensorMap& tw, const CUtensorMap& tx, LinearArgs& p, c
       p.x_slots = (p.k_blocks + s.split - 1) / s.split;
       smem = layout_linear<NT>(p);
       // the schedule has no second wave: all clusters must be resident at once
-      if (smem && p.split > 1 && max_active_clusters(kfn, smem, p.split) < p.clusters) smem = 0;
+      if (smem && p.split > 1 && max_active_clusters(kfn, smem, p.split, threads_for(NT)) < p.clusters) smem = 0;
       grid = p.clusters * p.split;
     }
   }
   if (!smem) {  // stream-K
     p.split = p.clusters = p.red_bufs = 0;
     grid = (int)std::min<long long>(grid_max, p.total_units);
+    if (NT >= 128) {
+      // prefill: grouped tile numbering; every full wave but the last runs
+      // whole tiles (one per CTA per wave, no partial-tile fix-up), and the
+      // last one to two waves' worth of tiles are split evenly by stream-K
+      p.raster_g = std::min(kRasterGroup, p.tiles / p.n_tiles);
+      const int waves = p.tiles / grid;
+      if (waves >= 2) p.dp_tiles = (waves - 1) * grid;
+      p.sk_units = p.total_units - (long long)p.dp_tiles * p.k_blocks;
+    }
     p.x_slots = (int)((p.total_units + grid - 1) / grid);
     smem = layout_linear<NT>(p);
     if (!smem)
       return fail(NPL_ERR_UNSUPPORTED, "npl_w8a8_linear: %d fp16 token tiles do not fit in shared memory",
                   p.x_slots);
   }
-  return launch_pdl_cluster("npl_w8a8_linear", kern, dim3((unsigned)grid), dim3(kThreads), (size_t)smem, st,
+  return launch_pdl_cluster("npl_w8a8_linear", kern, dim3((unsigned)grid), dim3(threads_for(NT)), (size_t)smem, st,
                             (unsigned)std::max(p.split, 1), tw, tx, p);
 }
 

@@ -186,9 +186,14 @@ def _rand_q(gen, *shape):
     return torch.randint(-127, 128, shape, generator=gen, dtype=torch.int8)
 
 
+# Prefill tiles (M > 64): 128- and 256-token tiles, two epilogue warpgroups.
+# (120, 40000, 128) and (2100, 8192, 256) have more than two waves of tiles, so
+# whole tiles run data-parallel before the stream-K tail; M = 2100 also has a
+# ragged raster group of token tiles (9 = 8 + 1) and a ragged last token tile.
 LINEAR_SHAPES = [
     (1, 384, 512), (3, 200, 768), (8, 12288, 4096), (8, 4096, 11008), (16, 1000, 512),
     (33, 640, 256), (64, 4096, 4096), (100, 512, 1024), (300, 384, 512), (8, 32003, 4096),
+    (200, 4096, 512), (120, 40000, 128), (2100, 8192, 256),
 ]
 
 
@@ -208,7 +213,8 @@ def test_linear_accumulators_and_dequant_bit_exact(K, m, n, k):
 
 
 @pytest.mark.parametrize("m,n,k", [(1, 4096, 4096), (8, 4096, 4096), (8, 4096, 11008), (64, 512, 1024), (5, 384, 256),
-                                   (300, 640, 512), (1100, 256, 256)])  # prefill tiles, ragged last tile
+                                   (300, 640, 512), (1100, 256, 256),  # prefill tiles, ragged last tile
+                                   (2100, 8192, 256)])  # data-parallel waves + stream-K tail
 def test_linear_residual_epilogue(K, m, n, k):
     gen = torch.Generator().manual_seed(m + n + k + 1)
     qa, qw = _rand_q(gen, m, k), _rand_q(gen, n, k)
@@ -223,7 +229,7 @@ def test_linear_residual_epilogue(K, m, n, k):
 
 
 @pytest.mark.parametrize("m,inter,k", [(1, 11008, 4096), (8, 11008, 4096), (64, 1024, 512), (5, 128, 256),
-                                       (300, 1024, 512)])
+                                       (300, 1024, 512), (2100, 4096, 256)])
 def test_linear_silu_mul_epilogue(K, m, inter, k):
     gen = torch.Generator().manual_seed(m + inter + k)
     qa = _rand_q(gen, m, k)
