@@ -451,7 +451,7 @@ __device__ __forceinline__ void silu_pair(const LinearArgs& p, LinearCtl& c, con
   epi_bar<NT>();
   const int col = n_tile * 64 + pr;
   __half* out = static_cast<__half*>(p.out);
-#pragma unroll
+#pragma unroll 1  // one copy of the 4-token SiLU body (instruction cache)
   for (int h = 0; h < 2; ++h) {
 #pragma unroll
     for (int jj = 0; jj < 4; ++jj) {

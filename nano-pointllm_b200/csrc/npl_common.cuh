@@ -132,21 +132,26 @@ __device__ __forceinline__ int quantize_one(float v, float s, float r) {
 // SiLU of an fp16 value g, rounded once to fp16 from the exact value:
 // fp16(g / (1 + e^-g)), the reference's act_fn(gate) on fp16 rows
 // (lightweight_runner.py:358) as the oracle states it (the fp64 formula
-// rounded once). Evaluated in fp32 first: y = RN(g / RN(1 + expf(-g))) is
-// within 3 fp32 ulps of the exact value (expf is documented at <= 2 ulps, the
-// add and the IEEE division round once each), so when y - d and y + d, with
-// d = 2^-19 |y| (four times that bound), round to the same fp16 value, so
-// does every value between them, the exact one included. Otherwise (a value
-// within ~2^-19 of an fp16 rounding midpoint, about 0.2% of inputs; zeros,
-// results below ~2^-40, non-finite g) the fp64 formula decides. The tests
-// check the result against the fp64 evaluation for every fp16 value.
-__device__ __forceinline__ float silu_f16_fp64(float g) {
+// rounded once). Evaluated in fp32 first: y = g / RN(1 + expf(-g)) with
+// __fdividef is within 5 fp32 ulps of the exact value (expf and __fdividef
+// are documented at <= 2 ulps each for these operands, the add rounds once),
+// so when y - d and y + d, with d = 2^-19 |y| (>= 16 ulps), round to the same
+// fp16 value, so does every value between them, the exact one included.
+// Otherwise (a value within ~2^-19 of an fp16 rounding midpoint, about 0.4% of
+// inputs; zeros, results below ~2^-40, g below -87 where __fdividef returns
+// 0, non-finite g) the fp64 formula decides. The tests check the result
+// against the fp64 evaluation for every fp16 value.
+// The fp64 fallback is a call, not inlined: the epilogues that evaluate SiLU
+// unroll it several times, and inlined copies of the fp64 exp overflow the
+// instruction cache ("no instruction" was the top warp stall of the prefill
+// gate/up launch).
+static __device__ __noinline__ float silu_f16_fp64(float g) {
   const double gd = (double)g;
   return __half2float(__double2half(gd / (1.0 + exp(-gd))));
 }
 
 __device__ __forceinline__ float silu_f16(float g) {
-  const float y = __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
+  const float y = __fdividef(g, __fadd_rn(1.0f, expf(-g)));
   const float d = fmaxf(fabsf(y) * 0x1p-19f, 0x1p-40f);
   const __half lo = __float2half_rn(__fsub_rn(y, d)), hi = __float2half_rn(__fadd_rn(y, d));
   if (__half_as_ushort(lo) == __half_as_ushort(hi) && isfinite(g)) return __half2float(lo);
