@@ -43,7 +43,7 @@ extern "C" {
 /* fused epilogues of npl_w8a8_linear / npl_w8a8_linear_ex */
 #define NPL_EPI_NONE 0     /* out = dequant(acc)                                  */
 #define NPL_EPI_RESIDUAL 1 /* out = fp16(fp16(dequant(acc)) + residual)           */
-#define NPL_EPI_SILU_MUL 2 /* gate/up rows tile-interleaved; out = silu(g) * u    */
+#define NPL_EPI_SILU_MUL 2 /* gate/up rows interleaved by 8; out = silu(g) * u    */
 #define NPL_EPI_ROPE_KV 3  /* packed QKV: RoPE on q/k, q -> q_out, k/v -> cache (npl_w8a8_linear_ex) */
 
 /* activation operand of npl_w8a8_linear_ex */
@@ -154,11 +154,11 @@ int npl_rmsnorm_quant(const void* x, const void* residual_or_null, const void* w
  * and the epilogue:
  *   NPL_EPI_NONE      out[m, n] = v as out_dtype (NPL_F32 or NPL_F16)
  *   NPL_EPI_RESIDUAL  out[m, n] = fp16(fp16(v) + residual[m, n])       (fp16)
- *   NPL_EPI_SILU_MUL  rows of qw are packed per 128-row tile t as 64 gate
- *                     rows [64t, 64t+64) then the matching 64 up rows; out is
- *                     [M, N/2] fp16 with out[m, j] = fp16(silu(g) * u),
- *                     g = fp16(v_gate), u = fp16(v_up), silu(g) = fp16 of
- *                     g / (1 + exp(-g)) evaluated in fp64.
+ *   NPL_EPI_SILU_MUL  rows of qw are packed in groups of 16: group j holds
+ *                     gate rows [8j, 8j+8) then the matching 8 up rows; out
+ *                     is [M, N/2] fp16 with out[m, i] = fp16(silu(g) * u),
+ *                     g = fp16(v_gate), u = fp16(v_up), silu(g) = g / (1 +
+ *                     exp(-g)) rounded once to fp16 from the exact value.
  * acc_out_or_null receives the int32 accumulators [M, N] (row stride N).
  * Replaces w8a8.py:118-139 integer_linear_per_output_reference and the
  * projection call sites paged_attention.py:97-124,283-305,1349-1352,1488 and

@@ -314,47 +314,6 @@ __device__ __forceinline__ void epilogue_chunk(const LinearArgs& p, LinearCtl& c
     for (int j = 0; j < 8; ++j)
       if (m_base + j < p.M) p.acc_out[(size_t)(m_base + j) * p.N + n] = acc[j];
   }
-  if (p.epilogue == NPL_EPI_SILU_MUL) {
-    // rows 0-63 gate, 64-127 up of output columns n_tile*64 + (row % 64).
-    // Gate row r and up row r + 64 split the chunk: the up row hands its
-    // values of tokens 0-3 to the gate row and the gate row its values of
-    // tokens 4-7 to the up row (one shared-memory exchange); each then
-    // finishes SiLU(g) * u for its 4 tokens, so all 128 threads work.
-    const float sw = e.sw;
-    const bool gate = row < 64;
-    const int pr = row & 63;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      if (gate == (j >= 4)) {
-        const int m = min(m_base + j, p.M - 1);
-        c.xchg[eg][j][gate ? 64 + pr : pr] = __float2half_rn(dequant(acc[j], sa[m], sw, p.bias, e.bias));
-      }
-    }
-    epi_bar<NT>();
-    const int col = n_tile * 64 + pr;
-    __half* out = static_cast<__half*>(p.out);
-#pragma unroll
-    for (int jj = 0; jj < 4; ++jj) {
-      const int j = gate ? jj : jj + 4;
-      const int m = m_base + j;
-      float h = 0.f;
-      if (m < p.M) {
-        const float own = __half2float(__float2half_rn(dequant(acc[j], sa[m], sw, p.bias, e.bias)));
-        const float other = __half2float(c.xchg[eg][j][gate ? pr : 64 + pr]);
-        const float g = gate ? own : other;
-        const float u = gate ? other : own;
-        const __half hh = __float2half_rn(__fmul_rn(silu_f16(g), u));
-        out[(size_t)m * p.ld_out + col] = hh;
-        h = fabsf(__half2float(hh));
-      }
-      if (p.absmax_out) {
-        h = warp_max(h);
-        if (lane == 0 && m < p.M) atomic_max_nonneg(p.absmax_out + m, h);
-      }
-    }
-    epi_bar<NT>();
-    return;
-  }
   if (p.epilogue == NPL_EPI_ROPE_KV) {
     // every tile lies in one of q | k | v (head blocks are multiples of 128)
     const int D = p.head_dim, half_d = D / 2;
@@ -415,65 +374,77 @@ __device__ __forceinline__ void epilogue_chunk(const LinearArgs& p, LinearCtl& c
   }
 }
 
-// SiLU * up epilogue of 16 token columns [c0, c0 + 16): two 8-token chunks
-// through ONE shared-memory exchange (two barriers per 16 tokens). In the
-// single-chunk epilogue each exchange row uses half its columns: [j][r] for
-// tokens j < 4 (up -> gate) and [j][64 + r] for j >= 4 (gate -> up). The
-// second chunk takes the other halves. Same arithmetic as epilogue_chunk.
-template <int NT>
-__device__ __forceinline__ void silu_pair(const LinearArgs& p, LinearCtl& c, const float* sa, int m_tile, int n_tile,
-                                          int row, int c0, const int32_t (&a0)[8], const int32_t (&a1)[8],
-                                          const EpiOperands& e) {
-  const int n = n_tile * kTileN + row;
-  const int m_base = m_tile * NT + c0;
+// SiLU * up epilogue of token columns [cb, ce) of a tile. Packed gate/up
+// layout (w8a8.pack_gate_up): per 128-row tile, 8 groups of 16 rows; rows
+// 16k .. 16k + 7 hold the gate rows of the tile's outputs 8k .. 8k + 7 and rows
+// 16k + 8 .. 16k + 15 the matching up rows. A 16x256b TMEM load gives thread
+// t of a warp lanes t/4 and t/4 + 8 of a 16-lane group at token columns
+// c0 + 2 (t % 4) and + 1, i.e. a gate row and its own up row, so every thread
+// finishes SiLU(g) * u for its outputs with no exchange between threads.
+// Warp quarter q holds groups 2q and 2q + 1 (h = 0, 1).
+// get_pairs(c0, h, v): v[0], v[1] = gate accumulators of this thread's two
+// token columns, v[2], v[3] = the up accumulators (see tmem_ld_16x256b).
+// Arithmetic per output: g = fp16(dequant(gate)), u = fp16(dequant(up)),
+// out = fp16(silu_f16(g) * u) -- lightweight_runner.py:358 on the fp16 gate/up
+// projections.
+template <int NT, typename PairFn>
+__device__ __forceinline__ void silu_tile(const LinearArgs& p, const float* sa, int m_tile, int n_tile, int cb,
+                                          int ce, PairFn&& get_pairs) {
   const int lane = threadIdx.x & 31;
-  const int eg = epi_group<NT>();
-  if (p.acc_out && n < p.N) {
+  const int q = (int)(threadIdx.x >> 5) & 3;
+  const int i = lane >> 2, e2 = 2 * (lane & 3);
+  float swg[2], swu[2], bg[2], bu[2];
+  int rg[2], col[2];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      if (m_base + j < p.M) p.acc_out[(size_t)(m_base + j) * p.N + n] = a0[j];
-      if (m_base + 8 + j < p.M) p.acc_out[(size_t)(m_base + 8 + j) * p.N + n] = a1[j];
-    }
-  }
-  const float sw = e.sw;
-  const bool gate = row < 64;
-  const int pr = row & 63;
-  const int s_mine = gate ? 64 + pr : pr;  // chunk 0 hand-over slot; chunk 1 uses the other half
-  const int s_other = gate ? pr : 64 + pr;
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    if (gate == (j >= 4)) {
-      const int m0 = min(m_base + j, p.M - 1), m1 = min(m_base + 8 + j, p.M - 1);
-      c.xchg[eg][j][s_mine] = __float2half_rn(dequant(a0[j], sa[m0], sw, p.bias, e.bias));
-      c.xchg[eg][j][s_other] = __float2half_rn(dequant(a1[j], sa[m1], sw, p.bias, e.bias));
-    }
-  }
-  epi_bar<NT>();
-  const int col = n_tile * 64 + pr;
-  __half* out = static_cast<__half*>(p.out);
-#pragma unroll 1  // one copy of the 4-token SiLU body (instruction cache)
   for (int h = 0; h < 2; ++h) {
+    rg[h] = n_tile * kTileN + 32 * q + 16 * h + i;  // gate row; its up row is rg + 8
+    col[h] = n_tile * 64 + 16 * q + 8 * h + i;      // output column
+    swg[h] = p.sw[rg[h]];
+    swu[h] = p.sw[rg[h] + 8];
+    bg[h] = p.bias ? p.bias[rg[h]] : 0.f;
+    bu[h] = p.bias ? p.bias[rg[h] + 8] : 0.f;
+  }
+  __half* out = static_cast<__half*>(p.out);
+  for (int c0 = cb; c0 < ce; c0 += 8) {
+    int32_t v[2][4];
+    get_pairs(c0, 0, v[0]);
+    get_pairs(c0, 1, v[1]);
+    const int m0 = m_tile * NT + c0 + e2;  // this thread's tokens m0, m0 + 1
+    if (p.acc_out) {
 #pragma unroll
-    for (int jj = 0; jj < 4; ++jj) {
-      const int j = gate ? jj : jj + 4;
-      const int m = m_base + 8 * h + j;
-      float a = 0.f;
-      if (m < p.M) {
-        const float own = __half2float(__float2half_rn(dequant(h ? a1[j] : a0[j], sa[m], sw, p.bias, e.bias)));
-        const float other = __half2float(c.xchg[eg][j][h ? s_mine : s_other]);
-        const float g = gate ? own : other;
-        const float u = gate ? other : own;
-        const __half hh = __float2half_rn(__fmul_rn(silu_f16(g), u));
-        out[(size_t)m * p.ld_out + col] = hh;
-        a = fabsf(__half2float(hh));
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int x = 0; x < 2; ++x)
+          if (m0 + x < p.M) {
+            p.acc_out[(size_t)(m0 + x) * p.N + rg[h]] = v[h][x];
+            p.acc_out[(size_t)(m0 + x) * p.N + rg[h] + 8] = v[h][2 + x];
+          }
+    }
+    float amax[2] = {0.f, 0.f};
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+#pragma unroll
+      for (int x = 0; x < 2; ++x) {
+        const int m = m0 + x;
+        if (m < p.M) {
+          const float g = __half2float(__float2half_rn(dequant(v[h][x], sa[m], swg[h], p.bias, bg[h])));
+          const float u = __half2float(__float2half_rn(dequant(v[h][2 + x], sa[m], swu[h], p.bias, bu[h])));
+          const __half hh = __float2half_rn(__fmul_rn(silu_f16(g), u));
+          out[(size_t)m * p.ld_out + col[h]] = hh;
+          amax[x] = fmaxf(amax[x], fabsf(__half2float(hh)));
+        }
       }
-      if (p.absmax_out) {
-        a = warp_max(a);
-        if (lane == 0 && m < p.M) atomic_max_nonneg(p.absmax_out + m, a);
+    }
+    if (p.absmax_out) {
+      // per token: the max over the 8 lanes that share it (same lane % 4)
+#pragma unroll
+      for (int x = 0; x < 2; ++x) {
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) amax[x] = fmaxf(amax[x], __shfl_xor_sync(0xffffffffu, amax[x], o));
+        if (i == 0 && m0 + x < p.M) atomic_max_nonneg(p.absmax_out + m0 + x, amax[x]);
       }
     }
   }
-  epi_bar<NT>();
 }
 
 // Residual epilogue of 8 token columns [c0, c0 + 8) of tile row `row`, with
@@ -505,19 +476,15 @@ __device__ __forceinline__ void residual_chunk(const LinearArgs& p, const float*
 // (the first 8 were loaded before the accumulator was ready), so a 256-token
 // prefill tile costs 8 residual round trips instead of 32. The other
 // epilogues keep a compact loop.
-template <int NT, typename AccFn>
+template <int NT, typename AccFn, typename PairFn>
 __device__ __forceinline__ void epilogue_tile(const LinearArgs& p, LinearCtl& c, const float* sa, int m_tile,
-                                              int n_tile, int row, const EpiOperands& e, AccFn&& get_acc) {
+                                              int n_tile, int row, const EpiOperands& e, AccFn&& get_acc,
+                                              PairFn&& get_pairs) {
   // this warpgroup's token columns [cb, ce)
   constexpr int kCols = NT / epi_groups_for(NT);
   const int cb = e.c_first, ce = cb + kCols;
-  if (NT >= 16 && p.epilogue == NPL_EPI_SILU_MUL) {
-    for (int c0 = cb; c0 < ce; c0 += 16) {
-      int32_t a0[8], a1[8];
-      get_acc(c0, a0);
-      get_acc(c0 + 8, a1);
-      silu_pair<NT>(p, c, sa, m_tile, n_tile, row, c0, a0, a1, e);
-    }
+  if (p.epilogue == NPL_EPI_SILU_MUL) {
+    silu_tile<NT>(p, sa, m_tile, n_tile, cb, ce, get_pairs);
     return;
   }
   if (p.epilogue != NPL_EPI_RESIDUAL) {
@@ -972,16 +939,29 @@ __global__ void __launch_bounds__(threads_for(NT), 1)
         if (leader) {
           if (ct == 0) mbar_arrive_expect_tx(&c.rfull[rb], (uint32_t)(p.split - 1) * red_bytes);
           mbar_wait_cluster(&c.rfull[rb], use & 1, p.status, NPL_DEV_TIMEOUT_EPILOGUE);
-          epilogue_tile<NT>(p, c, sa, m_tile, n_tile, row, eo, [&](int c0, int32_t(&acc)[8]) {
-            tmem_ld_x8(taddr + c0, acc);
-            tmem_wait_ld();
+          epilogue_tile<NT>(
+              p, c, sa, m_tile, n_tile, row, eo,
+              [&](int c0, int32_t(&acc)[8]) {
+                tmem_ld_x8(taddr + c0, acc);
+                tmem_wait_ld();
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              int32_t* cell = rbuf + (c0 + j) * kTileN + row;
-              acc[j] += *cell;  // int32 sums are exact in any order
-              *cell = 0;
-            }
-          });
+                for (int j = 0; j < 8; ++j) {
+                  int32_t* cell = rbuf + (c0 + j) * kTileN + row;
+                  acc[j] += *cell;  // int32 sums are exact in any order
+                  *cell = 0;
+                }
+              },
+              [&](int c0, int h, int32_t(&v)[4]) {
+                tmem_ld_16x256b(taddr + ((uint32_t)(16 * h) << 16) + (uint32_t)c0, v);
+                tmem_wait_ld();
+                const int r = 32 * quarter + 16 * h + (lane >> 2), cc = c0 + 2 * (lane & 3);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {  // (gate, up) x (cc, cc + 1); rows of this warp's quarter
+                  int32_t* cell = rbuf + (cc + (k & 1)) * kTileN + r + 8 * (k >> 1);
+                  v[k] += *cell;
+                  *cell = 0;
+                }
+              });
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&c.tempty[buf]);
@@ -1019,10 +999,16 @@ __global__ void __launch_bounds__(threads_for(NT), 1)
       }
       int32_t* ws = p.ws_acc + (size_t)slot * NT * kTileN;
       if (whole) {
-        epilogue_tile<NT>(p, c, sa, m_tile, n_tile, row, eo, [&](int c0, int32_t(&acc)[8]) {
-          tmem_ld_x8(taddr + c0, acc);
-          tmem_wait_ld();
-        });
+        epilogue_tile<NT>(
+            p, c, sa, m_tile, n_tile, row, eo,
+            [&](int c0, int32_t(&acc)[8]) {
+              tmem_ld_x8(taddr + c0, acc);
+              tmem_wait_ld();
+            },
+            [&](int c0, int h, int32_t(&v)[4]) {
+              tmem_ld_16x256b(taddr + ((uint32_t)(16 * h) << 16) + (uint32_t)c0, v);
+              tmem_wait_ld();
+            });
       } else {
         for (int c0 = c_first; c0 < c_first + NT / kEpiGroups; c0 += 8) {
           int32_t acc[8];
@@ -1042,14 +1028,25 @@ __global__ void __launch_bounds__(threads_for(NT), 1)
         if (ct == 0) c.last_flag = (atomic_add_acq_rel(p.ws_cnt + slot, kb1 - kb0) + (kb1 - kb0) == p.k_blocks);
         epi_all_bar(kEpiGroups);
         if (c.last_flag) {
-          epilogue_tile<NT>(p, c, sa, m_tile, n_tile, row, eo, [&](int c0, int32_t(&acc)[8]) {
+          epilogue_tile<NT>(
+              p, c, sa, m_tile, n_tile, row, eo,
+              [&](int c0, int32_t(&acc)[8]) {
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              int32_t* cell = ws + (size_t)(c0 + j) * kTileN + row;
-              acc[j] = __ldcg(cell);
-              __stcg(cell, 0);
-            }
-          });
+                for (int j = 0; j < 8; ++j) {
+                  int32_t* cell = ws + (size_t)(c0 + j) * kTileN + row;
+                  acc[j] = __ldcg(cell);
+                  __stcg(cell, 0);
+                }
+              },
+              [&](int c0, int h, int32_t(&v)[4]) {
+                const int r = 32 * quarter + 16 * h + (lane >> 2), cc = c0 + 2 * (lane & 3);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {  // (gate, up) x (cc, cc + 1)
+                  int32_t* cell = ws + (size_t)(cc + (k & 1)) * kTileN + r + 8 * (k >> 1);
+                  v[k] = __ldcg(cell);
+                  __stcg(cell, 0);
+                }
+              });
           if (ct == 0) p.ws_cnt[slot] = 0;
         }
         epi_all_bar(kEpiGroups);  // last_flag is read before the next tile sets it

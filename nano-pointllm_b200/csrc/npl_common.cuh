@@ -425,6 +425,15 @@ __device__ __forceinline__ void tmem_ld_x8(uint32_t taddr, int32_t (&r)[8]) {
                : "r"(taddr));
 }
 
+// 16 lanes x 8 columns (the 16x256b shape); thread i of the warp gets
+// r[0], r[1] = lane (base + i / 4), columns col + 2 (i % 4) and + 1, and
+// r[2], r[3] = the same columns of lane (base + 8 + i / 4).
+__device__ __forceinline__ void tmem_ld_16x256b(uint32_t taddr, int32_t (&r)[4]) {
+  asm volatile("tcgen05.ld.sync.aligned.16x256b.x1.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(taddr));
+}
+
 // 32 lanes x 32 consecutive 32-bit columns; thread i of the warp gets lane
 // (base lane + i), columns [col, col + 32).
 __device__ __forceinline__ void tmem_ld_x32(uint32_t taddr, uint32_t (&r)[32]) {

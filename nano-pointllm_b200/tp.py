@@ -7,7 +7,7 @@ configuration (one exchange per row-parallel linear):
 * column-parallel: the packed QKV projection (rank r owns q heads
   [r H/P, (r+1) H/P) and kv heads [r Hkv/P, ...), and the KV-pool slice of
   its kv heads), gate/up (rows [r I/P, ...) of gate and of up, each rank's
-  slice zero-padded to a multiple of 64 rows for the tile-interleaved
+  slice zero-padded to a multiple of 64 rows for the interleaved
   SiLU*up epilogue) and the LM head (vocab rows; logits all-gathered);
 * row-parallel: O and down. Their int8 input rows are split over the ranks,
   but the per-token scale is that of the WHOLE row (w8a8.py:106-115), so each

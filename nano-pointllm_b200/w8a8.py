@@ -136,7 +136,7 @@ def linear_q(qa: torch.Tensor, sa: torch.Tensor, qweight: torch.Tensor, wscale: 
     """int8 activations [M, K] (+ per-row fp32 scales) x int8 weight [N, K].
 
     epilogue NONE -> [M, N] out_dtype; RESIDUAL -> fp16(fp16(v) + residual);
-    SILU_MUL (qweight rows tile-interleaved, see pack_gate_up) -> [M, N/2] fp16.
+    SILU_MUL (qweight rows interleaved by 8, see pack_gate_up) -> [M, N/2] fp16.
     """
     _require_cuda(qa, sa, qweight, wscale, bias, residual)
     m, k = qa.shape
@@ -405,14 +405,17 @@ def silu_mul(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
 
 
 def pack_gate_up(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
-    """Row layout the SiLU*up epilogue reads: per 128-row tile t, gate rows
-    [64t, 64t+64) followed by up rows [64t, 64t+64). Works on weights [I, K]
-    or per-row scales [I]; I must be a multiple of 64."""
+    """Row layout the SiLU*up epilogue reads: groups of 16 rows, group j
+    holding gate rows [8j, 8j+8) followed by up rows [8j, 8j+8), so that a
+    128-row weight tile carries the gate and up rows of 64 outputs and one
+    16x256b TMEM load hands each epilogue thread a gate row together with its
+    up row. Works on weights [I, K] or per-row scales [I]; I must be a
+    multiple of 64 (whole 128-row tiles)."""
     inter = gate.shape[0]
     if inter % 64 or up.shape != gate.shape:
         raise ValueError("gate/up must match and have a multiple of 64 rows")
-    g = gate.reshape(inter // 64, 64, *gate.shape[1:])
-    u = up.reshape(inter // 64, 64, *up.shape[1:])
+    g = gate.reshape(inter // 8, 8, *gate.shape[1:])
+    u = up.reshape(inter // 8, 8, *up.shape[1:])
     return torch.stack([g, u], dim=1).reshape(2 * inter, *gate.shape[1:]).contiguous()
 
 

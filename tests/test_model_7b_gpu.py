@@ -231,10 +231,10 @@ def _decode_meta(bt, step: int, device):
 
 
 def _unpack_gate_up(rows: np.ndarray, inter: int) -> tuple[np.ndarray, np.ndarray]:
-    """Inverse of w8a8.pack_gate_up along the last axis: per 128 packed
-    columns, 64 gate then 64 up."""
+    """Inverse of w8a8.pack_gate_up along the last axis: per 16 packed
+    columns, 8 gate then 8 up."""
     lead = rows.shape[:-1]
-    t = rows.reshape(*lead, inter // 64, 2, 64)
+    t = rows.reshape(*lead, inter // 8, 2, 8)
     return t[..., 0, :].reshape(*lead, inter), t[..., 1, :].reshape(*lead, inter)
 
 
