@@ -109,6 +109,82 @@ __global__ void rope_store_kernel(const __half* __restrict__ qkv, int ld_qkv, in
   }
 }
 
+// The same with 16-byte accesses: one thread per (token, head, 8 pair
+// columns d .. d + 7 of the head's first half), so it moves 8 pairs per load
+// of x1, x2, cos and sin. Used when D % 16 == 0 and every row is 16-byte
+// aligned; same arithmetic per element as rope_store_kernel.
+__device__ __forceinline__ void h8_load(const __half* p, float (&v)[8]) {
+  const uint4 x = *reinterpret_cast<const uint4*>(p);
+  const __half2* h = reinterpret_cast<const __half2*>(&x);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __half22float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+
+__global__ void __launch_bounds__(256) rope_store_vec_kernel(const __half* __restrict__ qkv, int ld_qkv, int H,
+                                                             int Hkv, int D, const __half* __restrict__ cos_t,
+                                                             const __half* __restrict__ sin_t, int max_position,
+                                                             const int64_t* __restrict__ positions,
+                                                             const int32_t* __restrict__ slots,
+                                                             __half* __restrict__ q_out, __half* __restrict__ kc,
+                                                             __half* __restrict__ vc, long long num_slots,
+                                                             long long items, int* status) {
+  pdl_wait();
+  pdl_trigger();
+  const long long it = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (it >= items) return;
+  const int half_d = D / 2, chunks = half_d / 8, all_heads = H + 2 * Hkv;
+  const int d = (int)(it % chunks) * 8;
+  const int head = (int)((it / chunks) % all_heads);
+  const long long t = it / chunks / all_heads;
+  const long long pos = positions[t];
+  const long long slot = slots[t];
+  const bool pos_ok = pos >= 0 && pos < max_position;
+  const bool slot_ok = slot >= 0 && slot < num_slots;
+  if (head == 0 && d == 0 && (!pos_ok || slot >= num_slots)) flag_bad_index(status);
+  const __half* x = qkv + t * ld_qkv + (size_t)head * D;
+  if (head >= H + Hkv) {  // v
+    if (slot_ok) {
+      __half* vd = vc + (slot * Hkv + (head - H - Hkv)) * D;
+      *reinterpret_cast<uint4*>(vd + d) = *reinterpret_cast<const uint4*>(x + d);
+      *reinterpret_cast<uint4*>(vd + d + half_d) = *reinterpret_cast<const uint4*>(x + d + half_d);
+    }
+    return;
+  }
+  if (!pos_ok) return;
+  __half* dst;
+  if (head < H) {
+    dst = q_out + ((size_t)t * H + head) * D;
+  } else {
+    if (!slot_ok) return;
+    dst = kc + (slot * Hkv + (head - H)) * D;
+  }
+  float x1[8], x2[8], c1[8], c2[8], s1[8], s2[8];
+  h8_load(x + d, x1);
+  h8_load(x + d + half_d, x2);
+  h8_load(cos_t + pos * D + d, c1);
+  h8_load(cos_t + pos * D + d + half_d, c2);
+  h8_load(sin_t + pos * D + d, s1);
+  h8_load(sin_t + pos * D + d + half_d, s2);
+  uint4 o1, o2;
+  __half* h1 = reinterpret_cast<__half*>(&o1);
+  __half* h2 = reinterpret_cast<__half*>(&o2);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float a1 = __half2float(__float2half_rn(__fmul_rn(x1[i], c1[i])));
+    const float b1 = __half2float(__float2half_rn(__fmul_rn(-x2[i], s1[i])));
+    const float a2 = __half2float(__float2half_rn(__fmul_rn(x2[i], c2[i])));
+    const float b2 = __half2float(__float2half_rn(__fmul_rn(x1[i], s2[i])));
+    h1[i] = __float2half_rn(__fadd_rn(a1, b1));
+    h2[i] = __float2half_rn(__fadd_rn(a2, b2));
+  }
+  *reinterpret_cast<uint4*>(dst + d) = o1;
+  *reinterpret_cast<uint4*>(dst + d + half_d) = o2;
+}
+
 // ------------------------------------------------- paged decode attention
 // Persistent kernel, 3 CTAs per SM, 160 threads:
 //   warp 0     producer: takes work items (the CTA's first item is blockIdx.x,
@@ -1093,8 +1169,18 @@ extern "C" int npl_rope_store_kv(const void* qkv, int ld_qkv, int T, int H, int 
       max_position <= 0 || num_blocks <= 0 || block_size <= 0)
     return fail(NPL_ERR_ARG, "npl_rope_store_kv: bad shape");
   if (T == 0) return NPL_OK;
-  // decode batches: one head per CTA; larger batches: every head of a token
   const int all_heads = H + 2 * Hkv;
+  if (D % 16 == 0 && ld_qkv % 8 == 0 && aligned16(qkv) && aligned16(cos_table) && aligned16(sin_table) &&
+      aligned16(q_out) && aligned16(k_cache) && aligned16(v_cache)) {
+    const long long items = (long long)T * all_heads * (D / 16);
+    return launch_pdl("npl_rope_store_kv", rope_store_vec_kernel, dim3((unsigned)((items + 255) / 256)), dim3(256),
+                      0, static_cast<cudaStream_t>(stream), static_cast<const __half*>(qkv), ld_qkv, H, Hkv, D,
+                      static_cast<const __half*>(cos_table), static_cast<const __half*>(sin_table), max_position,
+                      positions, slot_mapping, static_cast<__half*>(q_out), static_cast<__half*>(k_cache),
+                      static_cast<__half*>(v_cache), (long long)num_blocks * block_size, items,
+                      device_status_ptr());
+  }
+  // decode batches: one head per CTA; larger batches: every head of a token
   const int hpc = T <= 64 ? 1 : all_heads;
   const int threads = T <= 64 ? D / 2 : std::min(512, ((all_heads * D / 2 + 31) / 32) * 32);
   return launch_pdl("npl_rope_store_kv", rope_store_kernel, dim3(T, (all_heads + hpc - 1) / hpc), dim3(threads), 0,

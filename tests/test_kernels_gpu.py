@@ -286,7 +286,8 @@ def test_linear_argument_errors(K):
 
 
 # ------------------------------------------------------------- RoPE / KV
-def test_rope_store_bit_exact(K):
+@pytest.mark.parametrize("pad", [0, 4])  # 0: 16-byte rows (vector kernel); 4: row stride not a multiple of 8
+def test_rope_store_bit_exact(K, pad):
     g = golden("rope.npz")
     t, h, d = g["q"].shape
     hkv = g["k"].shape[1]
@@ -297,11 +298,13 @@ def test_rope_store_bit_exact(K):
     cos[g["positions"]] = g["cos"]
     sin[g["positions"]] = g["sin"]
     qkv = np.concatenate([g["q"].reshape(t, -1), g["k"].reshape(t, -1), g["k"].reshape(t, -1) * 0.5], 1)
+    qkv_dev = torch.zeros(t, qkv.shape[1] + pad, dtype=torch.float16, device=K.dev)
+    qkv_dev[:, :qkv.shape[1]] = torch.from_numpy(qkv).to(K.dev)
     nb, bs = 4, 4
     kc = torch.zeros(nb, bs, hkv, d, dtype=torch.float16, device=K.dev)
     vc = torch.zeros_like(kc)
     slots = torch.tensor([3, 0, -1, 5, 6, 7, 8, 15], dtype=torch.int32, device=K.dev)
-    q = K.PA.rope_store_kvcache(torch.from_numpy(qkv).to(K.dev), h, hkv, d, torch.from_numpy(cos).to(K.dev),
+    q = K.PA.rope_store_kvcache(qkv_dev[:, :qkv.shape[1]], h, hkv, d, torch.from_numpy(cos).to(K.dev),
                                 torch.from_numpy(sin).to(K.dev), torch.from_numpy(g["positions"]).to(K.dev),
                                 slots, kc, vc)
     np.testing.assert_array_equal(cpu(q), g["q_rot"])
@@ -312,6 +315,27 @@ def test_rope_store_bit_exact(K):
         np.testing.assert_array_equal(kcn[s // bs, s % bs], g["k_rot"][i])
         np.testing.assert_array_equal(vcn[s // bs, s % bs], qkv[i, (h + hkv) * d:].reshape(hkv, d))
     assert float(kcn[0, 2].astype(np.float32).sum()) == 0.0  # slot 2 never written (padding row)
+
+
+def test_rope_store_vector_and_scalar_kernels_agree(K):
+    """Prefill-sized batch (300 tokens, GQA 8/2, D = 128): the 16-byte vector
+    kernel (contiguous rows) and the scalar kernel (row stride not a multiple
+    of 8) write identical q, k and v bits."""
+    gen = torch.Generator().manual_seed(11)
+    t, h, hkv, d, nb, bs = 300, 8, 2, 128, 24, 16
+    cols = (h + 2 * hkv) * d
+    qkv = (torch.randn(t, cols + 4, generator=gen) * 3).half().to(K.dev)
+    cos = torch.randn(512, d, generator=gen).half().to(K.dev)
+    sin = torch.randn(512, d, generator=gen).half().to(K.dev)
+    pos = torch.randint(0, 512, (t,), generator=gen).to(K.dev)
+    slots = torch.randperm(nb * bs, generator=gen)[:t].to(torch.int32).to(K.dev)
+    outs = []
+    for view in (qkv[:, :cols].contiguous(), qkv[:, :cols]):
+        kc = torch.zeros(nb, bs, hkv, d, dtype=torch.float16, device=K.dev)
+        vc = torch.zeros_like(kc)
+        outs.append((K.PA.rope_store_kvcache(view, h, hkv, d, cos, sin, pos, slots, kc, vc), kc, vc))
+    for a, b in zip(outs[0], outs[1]):
+        assert torch.equal(a.view(torch.int16), b.view(torch.int16))
 
 
 def test_store_kvcache_reference_cases(K):
