@@ -69,47 +69,74 @@ __device__ __forceinline__ void store_q<8>(int8_t* dst, const int (&q)[8]) {
 
 // absmax_in (float bits, optional): use this per-row absmax instead of the
 // row's own; absmax_out (optional): record the row's absmax; q == null:
-// record the absmax only.
-template <typename T>
-__global__ void __launch_bounds__(kQuantThreads) quant_rows_kernel(const T* __restrict__ x, int cols, int ldx,
-                                                                   int8_t* __restrict__ q, int ldq,
+// record the absmax only. A CTA handles R consecutive rows (R > 1 for long
+// batches, so that an SM keeps more rows in flight); each thread reads the
+// same chunks of every row, and a max does not depend on its order, so the
+// result is the same for any R.
+template <typename T, int R>
+__global__ void __launch_bounds__(kQuantThreads) quant_rows_kernel(const T* __restrict__ x, int rows, int cols,
+                                                                   int ldx, int8_t* __restrict__ q, int ldq,
                                                                    float* __restrict__ scale,
                                                                    const int32_t* __restrict__ absmax_in,
                                                                    int32_t* __restrict__ absmax_out) {
-  __shared__ float red[32];
+  __shared__ float red[R][32];
   constexpr int V = Vec<T>::N;
   pdl_wait();
-  const T* row = x + (size_t)blockIdx.x * ldx;
-  float amax = 0.f;
-  if (absmax_in) {
-    amax = __int_as_float(absmax_in[blockIdx.x]);
-  } else {
-#pragma unroll 2
-    for (int c = threadIdx.x * V; c < cols; c += kQuantThreads * V) {
-      float v[V];
-      Vec<T>::load(row + c, v);
+  const int r0 = blockIdx.x * R;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  float amax[R];
 #pragma unroll
-      for (int i = 0; i < V; ++i) amax = fmaxf(amax, fabsf(v[i]));
+  for (int r = 0; r < R; ++r) amax[r] = 0.f;
+  if (absmax_in) {
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+      if (r0 + r < rows) amax[r] = __int_as_float(absmax_in[r0 + r]);
+  } else {
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      if (r0 + r >= rows) continue;
+      const T* row = x + (size_t)(r0 + r) * ldx;
+#pragma unroll 2
+      for (int c = threadIdx.x * V; c < cols; c += kQuantThreads * V) {
+        float v[V];
+        Vec<T>::load(row + c, v);
+#pragma unroll
+        for (int i = 0; i < V; ++i) amax[r] = fmaxf(amax[r], fabsf(v[i]));
+      }
     }
-    amax = block_max(amax, red);
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      amax[r] = warp_max(amax[r]);
+      if (lane == 0) red[r][warp] = amax[r];
+    }
+    __syncthreads();
+#pragma unroll
+    for (int r = 0; r < R; ++r) amax[r] = warp_max(lane < kQuantThreads / 32 ? red[r][lane] : 0.f);
   }
-  if (absmax_out && threadIdx.x == 0) absmax_out[blockIdx.x] = __float_as_int(amax);
+#pragma unroll
+  for (int r = 0; r < R; ++r)
+    if (absmax_out && threadIdx.x == 0 && r0 + r < rows) absmax_out[r0 + r] = __float_as_int(amax[r]);
   if (!q) {
     pdl_trigger();
     return;
   }
-  const float s = scale_from_absmax(amax);
-  const float rs = quant_recip(s);
-  if (threadIdx.x == 0) scale[blockIdx.x] = s;
-  int8_t* qrow = q + (size_t)blockIdx.x * ldq;
-#pragma unroll 2
-  for (int c = threadIdx.x * V; c < cols; c += kQuantThreads * V) {
-    float v[V];
-    Vec<T>::load(row + c, v);
-    int qi[V];
 #pragma unroll
-    for (int i = 0; i < V; ++i) qi[i] = quantize_one(v[i], s, rs);
-    store_q<V>(qrow + c, qi);
+  for (int r = 0; r < R; ++r) {
+    if (r0 + r >= rows) continue;
+    const float s = scale_from_absmax(amax[r]);
+    const float rs = quant_recip(s);
+    if (threadIdx.x == 0) scale[r0 + r] = s;
+    const T* row = x + (size_t)(r0 + r) * ldx;
+    int8_t* qrow = q + (size_t)(r0 + r) * ldq;
+#pragma unroll 2
+    for (int c = threadIdx.x * V; c < cols; c += kQuantThreads * V) {
+      float v[V];
+      Vec<T>::load(row + c, v);
+      int qi[V];
+#pragma unroll
+      for (int i = 0; i < V; ++i) qi[i] = quantize_one(v[i], s, rs);
+      store_q<V>(qrow + c, qi);
+    }
   }
   pdl_trigger_after_writes();  // the rows may be weights, read by the next linear before its pdl_wait
 }
@@ -303,12 +330,17 @@ int quant_rows_common(const char* what, const void* x, int x_dtype, int rows, in
   if (!aligned16(x) || (q && !aligned16(q))) return fail(NPL_ERR_ARG, "%s: pointers must be 16-byte aligned", what);
   if (rows == 0) return NPL_OK;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // decode batches: a CTA per row; longer batches: 4 rows per CTA
+  const bool multi = rows > 64;
+  const dim3 grid(multi ? (rows + 3) / 4 : rows);
   if (x_dtype == NPL_F32)
-    return launch_pdl(what, quant_rows_kernel<float>, dim3(rows), dim3(kQuantThreads), 0, st,
-                      static_cast<const float*>(x), cols, ldx, q, ldq, scale, absmax_in, absmax_out);
+    return launch_pdl(what, multi ? quant_rows_kernel<float, 4> : quant_rows_kernel<float, 1>, grid,
+                      dim3(kQuantThreads), 0, st, static_cast<const float*>(x), rows, cols, ldx, q, ldq, scale,
+                      absmax_in, absmax_out);
   if (x_dtype == NPL_F16)
-    return launch_pdl(what, quant_rows_kernel<__half>, dim3(rows), dim3(kQuantThreads), 0, st,
-                      static_cast<const __half*>(x), cols, ldx, q, ldq, scale, absmax_in, absmax_out);
+    return launch_pdl(what, multi ? quant_rows_kernel<__half, 4> : quant_rows_kernel<__half, 1>, grid,
+                      dim3(kQuantThreads), 0, st, static_cast<const __half*>(x), rows, cols, ldx, q, ldq, scale,
+                      absmax_in, absmax_out);
   return fail(NPL_ERR_ARG, "%s: x_dtype must be NPL_F32 or NPL_F16", what);
 }
 

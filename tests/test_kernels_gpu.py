@@ -35,7 +35,8 @@ def cpu(t: torch.Tensor) -> np.ndarray:
 
 # ------------------------------------------------------------ quantisation
 @pytest.mark.parametrize("dtype", [torch.float32, torch.float16])
-@pytest.mark.parametrize("rows,cols", [(8, 4096), (5, 768), (1, 16), (64, 11008), (3, 48)])
+@pytest.mark.parametrize("rows,cols", [(8, 4096), (5, 768), (1, 16), (64, 11008), (3, 48),
+                                       (300, 4096), (1001, 11008)])  # > 64 rows: 4 rows per CTA
 def test_quant_rows_bit_exact(K, dtype, rows, cols):
     g = torch.Generator().manual_seed(rows * 7 + cols)
     x = torch.randn(rows, cols, generator=g) * 3
@@ -136,7 +137,8 @@ def test_rmsnorm_quant_bit_exact_and_reference_bound(K):
         assert d.max() <= 1 and (d > 0).sum() <= 0.0005 * d.size
 
 
-@pytest.mark.parametrize("rows,cols", [(1, 4096), (8, 4096), (64, 4096), (3, 512), (8, 11008)])
+@pytest.mark.parametrize("rows,cols", [(1, 4096), (8, 4096), (64, 4096), (3, 512), (8, 11008),
+                                       (301, 4096), (130, 11008), (70, 20000)])  # prefill-sized batches
 def test_rmsnorm_quant_shapes(K, rows, cols):
     gen = torch.Generator().manual_seed(cols + rows)
     x = torch.randn(rows, cols, generator=gen).half()
@@ -147,6 +149,9 @@ def test_rmsnorm_quant_shapes(K, rows, cols):
     np.testing.assert_array_equal(cpu(summed), suo)
     np.testing.assert_array_equal(cpu(q), qo)
     np.testing.assert_array_equal(cpu(s), so)
+    if rows > 64:  # the same rows in a decode-sized batch (one row per CTA): identical bits
+        q8, s8, _ = K.R.rmsnorm_quant(x[:8].to(K.dev), w.to(K.dev), 1e-6, r[:8].to(K.dev))
+        assert torch.equal(q8.cpu(), q[:8].cpu()) and torch.equal(s8.cpu(), s[:8].cpu())
 
 
 # ------------------------------------------------------------------ linear
