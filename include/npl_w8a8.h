@@ -207,6 +207,13 @@ typedef struct npl_rope_kv {
  * Epilogues: those of npl_w8a8_linear, plus
  *   NPL_EPI_SILU_MUL with absmax_out: absmax_out[m] (float bits, zero before
  *                      the call) receives max over the row of |out[m, :]|.
+ *                      With q_out / q_scale as well (M <= 64): once every CTA
+ *                      has stored its outputs, the kernel quantises out per
+ *                      token (npl_quant_rows' arithmetic) into q_out int8
+ *                      [M, N/2] (row stride N/2, 8-byte aligned) and q_scale
+ *                      fp32 [M], and leaves absmax_out zero again: the down
+ *                      projection's input without a separate launch. Needs
+ *                      ld_out % 8 == 0 and a 16-byte aligned out.
  *   NPL_EPI_ROPE_KV    N = (heads + 2 kv_heads) * head_dim (packed q | k | v,
  *                      head blocks multiples of 128 rows): q and k get RoPE
  *                      exactly as npl_rope_store_kv; q -> rope.q_out; k and v
@@ -241,6 +248,8 @@ typedef struct npl_linear_args {
   int32_t* acc_out;
   int32_t* absmax_out;
   npl_rope_kv rope;
+  int8_t* q_out;   /* NPL_EPI_SILU_MUL with absmax_out, M <= 64: out quantised per token (see below) */
+  float* q_scale;
 } npl_linear_args;
 
 int npl_w8a8_linear_ex(const npl_linear_args* args, void* workspace, size_t workspace_bytes, void* stream);

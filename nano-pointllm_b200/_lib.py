@@ -51,7 +51,7 @@ class NplLinearArgs(ctypes.Structure):
                 ("x_absmax", _P), ("norm_weight", _P), ("eps", _F), ("qw", _P), ("ldw", _I), ("sw", _P),
                 ("bias", _P), ("M", _I), ("N", _I), ("K", _I), ("epilogue", _I), ("residual", _P), ("ld_res", _I),
                 ("out", _P), ("ld_out", _I), ("out_dtype", _I), ("acc_out", _P), ("absmax_out", _P),
-                ("rope", NplRopeKV)]
+                ("rope", NplRopeKV), ("q_out", _P), ("q_scale", _P)]
 
 
 TP_MAX_RANKS = 8

@@ -90,6 +90,8 @@ struct LinearArgs {
   int out_dtype;
   int32_t* acc_out;
   int32_t* absmax_out;     // NPL_EPI_SILU_MUL: per-token max |out| (float bits), atomic max
+  int8_t* silu_q;          // NPL_EPI_SILU_MUL with absmax_out: per-token int8 of out [M, N/2] (row stride N/2)
+  float* silu_qs;          //   and its scales [M], written after every CTA has stored its outputs
   const __half* cos_t;     // NPL_EPI_ROPE_KV
   const __half* sin_t;
   int max_position;
@@ -116,6 +118,7 @@ struct LinearArgs {
   int32_t* ws_acc;   // [grid - 1 slots][NT][128]
   int32_t* ws_cnt;   // [grid - 1 slots]
   int32_t* ws_xcnt;  // [1]: CTAs done reading x_absmax
+  int32_t* ws_gcnt;  // [2]: CTAs arrived at / done after the grid-wide step of silu_q
   int* status;
 };
 
@@ -700,6 +703,70 @@ __device__ void produce_activations(const LinearArgs& p, int8_t* xslot, float* s
   fence_proxy_async_smem();  // the tensor cores read these tiles through the async proxy
 }
 
+__device__ __forceinline__ int ld_acquire_gpu(const int32_t* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// SiLU * up with silu_q: after every CTA of the grid has stored its outputs
+// and their per-token absmax (a grid-wide count: every CTA of the grid is
+// resident at once, since the grid has at most one CTA per SM or, under
+// cluster split-K, only as many clusters as fit at once, and the next kernel
+// can launch only after all of them have started), every CTA
+// quantises an interleaved share of the [M, N/2] rows per token, exactly as
+// npl_quant_rows would (w8a8.py:106-115), so that the down projection takes
+// int8 rows without a separate quantisation launch. The last CTA done
+// clears the absmax words and both counts for the next call. Run by every
+// epilogue thread of the CTA.
+template <int NT>
+__device__ void silu_quant_rows(const LinearArgs& p, LinearCtl& c, int ct) {
+  constexpr int kGroups = epi_groups_for(NT);
+  constexpr int kThr = 128 * kGroups;
+  epi_all_bar(kGroups);  // this CTA's outputs and absmax atomics are issued
+  if (ct == 0) {
+    __threadfence();
+    atomicAdd(p.ws_gcnt, 1);
+    const uint64_t t0 = globaltimer_ns();
+    int ok = 1;
+    while (ld_acquire_gpu(p.ws_gcnt) < (int)gridDim.x) {
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        atomicCAS(p.status, 0, (int)NPL_DEV_TIMEOUT_EPILOGUE);
+        ok = 0;
+        break;
+      }
+    }
+    c.last_flag = ok;
+  }
+  epi_all_bar(kGroups);
+  if (!c.last_flag) return;  // the status word reports it
+  const int cols = p.N / 2, chunks_per_row = cols / 8;
+  const int chunks = p.M * chunks_per_row;
+  __half* out = static_cast<__half*>(p.out);
+  for (int i = (int)blockIdx.x * kThr + ct; i < chunks; i += (int)gridDim.x * kThr) {
+    const int m = i / chunks_per_row, c0 = (i - m * chunks_per_row) * 8;
+    const float sc = scale_from_absmax(__int_as_float(__ldcg(p.absmax_out + m)));
+    const float rs = quant_recip(sc);
+    const uint4 v = __ldcg(reinterpret_cast<const uint4*>(out + (size_t)m * p.ld_out + c0));
+    const __half* h = reinterpret_cast<const __half*>(&v);
+    uint2 qv;
+    uint32_t* w = reinterpret_cast<uint32_t*>(&qv);
+    w[0] = w[1] = 0;
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      w[e / 4] |= (uint32_t)(quantize_one(__half2float(h[e]), sc, rs) & 0xff) << (8 * (e % 4));
+    *reinterpret_cast<uint2*>(p.silu_q + (size_t)m * cols + c0) = qv;
+  }
+  if (blockIdx.x == 0)
+    for (int m = ct; m < p.M; m += kThr) p.silu_qs[m] = scale_from_absmax(__int_as_float(__ldcg(p.absmax_out + m)));
+  epi_all_bar(kGroups);  // every read of the absmax words before the done count
+  if (ct == 0 && atomic_add_acq_rel(p.ws_gcnt + 1, 1) + 1 == (int)gridDim.x) {
+    for (int m = 0; m < p.M; ++m) atomicExch(p.absmax_out + m, 0);
+    atomicExch(p.ws_gcnt, 0);
+    atomicExch(p.ws_gcnt + 1, 0);
+  }
+}
+
 // kXF16: the fp16-activation modes (their prologue costs registers, so the
 // int8-activation kernel is compiled without it).
 template <int NT, bool kXF16>
@@ -1053,6 +1120,7 @@ __global__ void __launch_bounds__(threads_for(NT), 1)
       }
       ++seg;
     }
+    if (p.silu_q) silu_quant_rows<NT>(p, c, ct);
   }
 
   tc_fence_before();
@@ -1118,7 +1186,7 @@ size_t ws_acc_bytes(int M) {
 
 size_t ws_bytes(int M) {
   const size_t slots = (size_t)std::max(1, max_grid() - 1);
-  return ws_acc_bytes(M) + (((slots + 1) * sizeof(int32_t) + 255) & ~size_t(255));
+  return ws_acc_bytes(M) + (((slots + 3) * sizeof(int32_t) + 255) & ~size_t(255));
 }
 
 constexpr uint32_t align1k(size_t x) { return (uint32_t)((x + 1023) & ~size_t(1023)); }
@@ -1302,6 +1370,8 @@ struct LinearCall {
   int32_t* acc_out;
   int32_t* absmax_out;
   const npl_rope_kv* rope;
+  int8_t* silu_q;
+  float* silu_qs;
 };
 
 int run_linear(const LinearCall& a, void* workspace, size_t workspace_bytes, void* stream) {
@@ -1333,6 +1403,11 @@ int run_linear(const LinearCall& a, void* workspace, size_t workspace_bytes, voi
   } else if (a.epilogue == NPL_EPI_SILU_MUL) {
     if (!a.out || N % kTileN || a.out_dtype != NPL_F16 || a.ld_out < N / 2)
       return fail(NPL_ERR_ARG, "npl_w8a8_linear: SiLU*up epilogue needs N %% 128 == 0, fp16 out, ld_out >= N/2");
+    if (a.silu_q && (!a.silu_qs || !a.absmax_out || M > 64 || a.ld_out % 8 || !aligned16(a.out) ||
+                     (reinterpret_cast<uintptr_t>(a.silu_q) & 7u)))
+      return fail(NPL_ERR_ARG,
+                  "npl_w8a8_linear: q_out needs q_scale, absmax_out, M <= 64, ld_out %% 8 == 0, a 16-byte aligned "
+                  "out and an 8-byte aligned q_out");
   } else if (a.epilogue == NPL_EPI_NONE) {
     if (!a.out || (a.out_dtype != NPL_F16 && a.out_dtype != NPL_F32) || a.ld_out < N)
       return fail(NPL_ERR_ARG, "npl_w8a8_linear: out_dtype must be NPL_F16/NPL_F32 and ld_out >= N");
@@ -1376,6 +1451,8 @@ int run_linear(const LinearCall& a, void* workspace, size_t workspace_bytes, voi
   p.out_dtype = a.out_dtype;
   p.acc_out = a.acc_out;
   p.absmax_out = a.absmax_out;
+  p.silu_q = a.silu_q;
+  p.silu_qs = a.silu_qs;
   if (a.epilogue == NPL_EPI_ROPE_KV) {
     const npl_rope_kv* r = a.rope;
     p.cos_t = static_cast<const __half*>(r->cos_table);
@@ -1394,6 +1471,7 @@ int run_linear(const LinearCall& a, void* workspace, size_t workspace_bytes, voi
   p.ws_acc = static_cast<int32_t*>(workspace);
   p.ws_cnt = reinterpret_cast<int32_t*>(static_cast<char*>(workspace) + ws_acc_bytes(M));
   p.ws_xcnt = p.ws_cnt + std::max(1, max_grid() - 1);
+  p.ws_gcnt = p.ws_xcnt + 1;
   p.n_tiles = (N + kTileN - 1) / kTileN;
   p.k_blocks = (K + kBlockK - 1) / kBlockK;
   const int m_tiles = (M + nt - 1) / nt;
@@ -1489,6 +1567,8 @@ extern "C" int npl_w8a8_linear_ex(const npl_linear_args* args, void* workspace, 
   a.acc_out = args->acc_out;
   a.absmax_out = args->absmax_out;
   a.rope = &args->rope;
+  a.silu_q = args->q_out;
+  a.silu_qs = args->q_scale;
   return run_linear(a, workspace, workspace_bytes, stream);
 }
 

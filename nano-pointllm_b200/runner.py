@@ -139,7 +139,7 @@ class W8A8LlamaRunner:
 
     def __init__(self, shape: LlamaShape, state_dict: dict[str, torch.Tensor], *, device: torch.device,
                  kv_pool: torch.Tensor | None = None, num_blocks: int = 0, block_size: int = 256,
-                 fuse_mlp_quant: bool = False, forward_context=None):
+                 fuse_mlp_quant: bool = False, fuse_silu_quant: bool = False, forward_context=None):
         """``forward_context``: a callable returning the current step's
         context. Default: this module's get_forward_context. The reference
         engine passes its own nanopointllm.engine.forward_context.
@@ -155,6 +155,14 @@ class W8A8LlamaRunner:
         # them. Off by default: on B200 the in-kernel quantisation lengthens
         # down's critical path by more than the separate kernel costs.
         self.fuse_mlp_quant = fuse_mlp_quant
+        # fuse_silu_quant, decode batches: the gate/up launch also quantises
+        # SiLU(gate)*up per token once all of its CTAs have stored their
+        # outputs (a grid-wide count), so down takes int8 rows with no
+        # quantisation launch between them; bit-identical to the separate
+        # kernel. Off by default: on B200 the grid-wide wait and the extra
+        # pass lengthen gate/up by as much as the separate launch costs
+        # (decode step 3.289 ms against 3.279).
+        self.fuse_silu_quant = fuse_silu_quant
         self._act_absmax = torch.zeros(64, dtype=torch.int32, device=self.device)
         if kv_pool is None:
             kv_pool = torch.zeros(2, shape.layers, num_blocks, block_size, shape.kv_heads, shape.head_dim,
@@ -276,6 +284,15 @@ class W8A8LlamaRunner:
                      m=m, qa=xq, sa=xs, epilogue=L.EPI_SILU_MUL, absmax_out=self._act_absmax)
             return op("linear.down", W.linear_ex, layer.down.qweight, layer.down.wscale, x_mode=L.X_F16_ABSMAX,
                       m=m, x_f16=act, x_absmax=self._act_absmax, epilogue=L.EPI_RESIDUAL, residual=h2)
+        if self.fuse_silu_quant and m <= self._act_absmax.numel():
+            inter = layer.gate_up.qweight.shape[0] // 2
+            aq = torch.empty((m, inter), dtype=torch.int8, device=h2.device)
+            asc = torch.empty(m, dtype=torch.float32, device=h2.device)
+            # the absmax buffer is zero on entry and zeroed again by the launch
+            op("linear.gate_up", W.linear_ex, layer.gate_up.qweight, layer.gate_up.wscale, x_mode=L.X_INT8, m=m,
+               qa=xq, sa=xs, epilogue=L.EPI_SILU_MUL, absmax_out=self._act_absmax, q_out=aq, q_scale=asc)
+            return op("linear.down", W.linear_q, aq, asc, layer.down.qweight, layer.down.wscale,
+                      epilogue=L.EPI_RESIDUAL, residual=h2)
         act = op("linear.gate_up", W.linear_q, xq, xs, layer.gate_up.qweight, layer.gate_up.wscale,
                  epilogue=L.EPI_SILU_MUL)
         aq, asc = op("quant", W.dynamic_per_token_quant, act)

@@ -163,13 +163,16 @@ def linear_ex(qweight: torch.Tensor, wscale: torch.Tensor, *, x_mode: int, m: in
               norm_weight: torch.Tensor | None = None, eps: float = 1e-6, bias: torch.Tensor | None = None,
               epilogue: int = L.EPI_NONE, residual: torch.Tensor | None = None, out: torch.Tensor | None = None,
               out_dtype: torch.dtype = torch.float16, acc_out: torch.Tensor | None = None,
-              absmax_out: torch.Tensor | None = None, rope: dict | None = None) -> torch.Tensor | None:
+              absmax_out: torch.Tensor | None = None, rope: dict | None = None,
+              q_out: torch.Tensor | None = None, q_scale: torch.Tensor | None = None) -> torch.Tensor | None:
     """npl_w8a8_linear_ex: the decode linear with its activation preparation
     (int8 / fp16 + given absmax / fp16 + RMSNorm) and epilogue (dequant,
     residual, SiLU*up (+ absmax), RoPE + KV store) in one kernel.
 
     ``rope`` (for EPI_ROPE_KV): dict with cos, sin, positions, slots, q_out,
-    k_cache, v_cache, heads, kv_heads, head_dim. Returns ``out`` (None for
+    k_cache, v_cache, heads, kv_heads, head_dim. ``q_out`` / ``q_scale`` (for
+    EPI_SILU_MUL with ``absmax_out``, m <= 64): the output quantised per token
+    in the same launch (int8 [m, n/2], fp32 [m]). Returns ``out`` (None for
     EPI_ROPE_KV, whose outputs are rope["q_out"] and the caches).
     """
     n, k = qweight.shape
@@ -195,6 +198,7 @@ def linear_ex(qweight: torch.Tensor, wscale: torch.Tensor, *, x_mode: int, m: in
         a.out, a.ld_out, a.out_dtype = out.data_ptr(), out.stride(0), _DT[out.dtype]
     a.acc_out = L.ptr(acc_out)
     a.absmax_out = L.ptr(absmax_out)
+    a.q_out, a.q_scale = L.ptr(q_out), L.ptr(q_scale)
     if rope is not None:
         r = a.rope
         r.cos_table, r.sin_table = rope["cos"].data_ptr(), rope["sin"].data_ptr()

@@ -158,3 +158,40 @@ def test_fp16_activations_limited_to_decode_batches(K):
     x = torch.zeros(65, 256, dtype=torch.float16, device=K.dev)
     with pytest.raises(K.lib.NplError):
         K.W.linear_ex(qw, sw, x_mode=K.lib.X_F16_RMSNORM, m=65, x_f16=x, norm_weight=torch.ones(256).half().to(K.dev))
+
+
+@pytest.mark.parametrize("m", [1, 8, 33, 64])
+def test_gate_up_quantises_its_output_in_the_same_launch(K, m):
+    """Packed gate/up with q_out / q_scale: after all of its CTAs have stored
+    SiLU(gate)*up, the launch quantises the rows per token itself. The int8
+    rows and scales equal npl_quant_rows on the fp16 output (and the oracle),
+    on two calls in a row (the grid-wide counts and the absmax words are left
+    zero for the next call)."""
+    from nanopointllm_b200 import synthetic as S
+    x, _, nw, gate, up, _ = S.mlp_block_inputs(m, seed=2)
+    qg, sg = O.per_output_weight_quant(gate.numpy())
+    qu, su = O.per_output_weight_quant(up.numpy())
+    dev = K.dev
+    packed_w = K.W.pack_gate_up(torch.from_numpy(qg), torch.from_numpy(qu)).to(dev)
+    packed_s = K.W.pack_gate_up(torch.from_numpy(sg), torch.from_numpy(su)).to(dev)
+    q8, s8, _, _ = O.rmsnorm_quant(x.numpy(), nw.numpy(), 1e-6)
+    g16, _ = O.w8a8_linear(q8, s8, qg, sg)
+    u16, _ = O.w8a8_linear(q8, s8, qu, su)
+    h = O.silu_mul(g16, u16)
+    hq, hs = O.dynamic_per_token_quant(h)
+    amax = torch.zeros(64, dtype=torch.int32, device=dev)
+    inter = gate.shape[0]
+    for _ in range(2):
+        aq = torch.full((m, inter), 99, dtype=torch.int8, device=dev)
+        asc = torch.zeros(m, dtype=torch.float32, device=dev)
+        act = K.W.linear_ex(packed_w, packed_s, x_mode=K.lib.X_INT8, m=m, qa=torch.from_numpy(q8).to(dev),
+                            sa=torch.from_numpy(s8).to(dev), epilogue=K.lib.EPI_SILU_MUL, absmax_out=amax,
+                            q_out=aq, q_scale=asc)
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(cpu(act), h)
+        np.testing.assert_array_equal(cpu(aq), hq)
+        np.testing.assert_array_equal(cpu(asc), hs.reshape(-1))
+        sq, ss = K.W.dynamic_per_token_quant(act)
+        assert torch.equal(sq, aq) and torch.equal(ss.reshape(-1), asc)
+        assert int(amax.count_nonzero()) == 0
+    K.lib.device_status()

@@ -101,20 +101,32 @@ def _recorder(device):
 
 
 def _parse(rec, n_layers: int):
-    """Per-layer tensors of a recorded forward, in either op structure of
-    the runner: nine kernels per layer (RMSNorm+quant, QKV, RoPE + KV store,
+    """Per-layer tensors of a recorded forward, in any op structure of the
+    runner: nine kernels per layer (RMSNorm+quant, QKV, RoPE + KV store,
     attention, O, RMSNorm+quant, gate/up, quant, down; then the final norm
-    and the LM head), or the decode structure whose O, gate/up and down also
-    produce the next linear's int8 input (next_q / next_scale): one
-    RMSNorm+quant before layer 0, six kernels per layer, the LM head."""
+    and the LM head); eight, when the gate/up launch also quantises its
+    output (q_out / q_scale, decode batches: no separate quant); or the
+    structure whose O, gate/up and down also produce the next linear's int8
+    input (next_q / next_scale): one RMSNorm+quant before layer 0, six
+    kernels per layer, the LM head."""
     names = [r[0] for r in rec]
-    fused = "quant" not in names
-    per = ["linear.qkv", "rope_store", "attention", "linear.o", "linear.gate_up", "linear.down"] if fused else \
-        ["rmsnorm_quant", "linear.qkv", "rope_store", "attention", "linear.o", "rmsnorm_quant", "linear.gate_up",
-         "quant", "linear.down"]
-    want = (["rmsnorm_quant"] + per * n_layers + ["linear.lm_head"]) if fused else \
+    if "quant" in names:
+        mode = "separate"
+    elif names.count("rmsnorm_quant") == 2 * n_layers + 1:
+        mode = "silu_q"
+    else:
+        mode = "next_q"
+    per = {
+        "separate": ["rmsnorm_quant", "linear.qkv", "rope_store", "attention", "linear.o", "rmsnorm_quant",
+                     "linear.gate_up", "quant", "linear.down"],
+        "silu_q": ["rmsnorm_quant", "linear.qkv", "rope_store", "attention", "linear.o", "rmsnorm_quant",
+                   "linear.gate_up", "linear.down"],
+        "next_q": ["linear.qkv", "rope_store", "attention", "linear.o", "linear.gate_up", "linear.down"],
+    }[mode]
+    want = (["rmsnorm_quant"] + per * n_layers + ["linear.lm_head"]) if mode == "next_q" else \
         (per * n_layers + ["rmsnorm_quant", "linear.lm_head"])
     assert names == want, names
+    fused = mode == "next_q"
     it = iter(rec)
     layers, nxt = [], None
     if fused:
@@ -138,6 +150,8 @@ def _parse(rec, n_layers: int):
         _, _, kw, L["act"], L["gu_acc"] = next(it)
         if fused:
             L["mq"], L["ms"] = kw["next_q"], kw["next_scale"]
+        elif mode == "silu_q":
+            L["mq"], L["ms"] = kw["q_out"], kw["q_scale"]
         else:
             _, _, _, (L["mq"], L["ms"]), _ = next(it)
         _, _, kw, L["h_next"], L["d_acc"] = next(it)
@@ -325,8 +339,8 @@ def test_7b_decode_step_every_layer(cuda_device):
             quant[p + "self_attn." + n + ".weight"] = (qq[a:b], qs[a:b])
         quant[p + "self_attn.o_proj.weight"] = (cpu(layer.o.qweight), cpu(layer.o.wscale))
         gq, gs = cpu(layer.gate_up.qweight), cpu(layer.gate_up.wscale)
-        gq = gq.reshape(shape.intermediate // 64, 2, 64, -1)
-        gs = gs.reshape(shape.intermediate // 64, 2, 64)
+        gq = gq.reshape(shape.intermediate // 8, 2, 8, -1)  # w8a8.pack_gate_up: 8 gate rows, then their 8 up rows
+        gs = gs.reshape(shape.intermediate // 8, 2, 8)
         quant[p + "mlp.gate_proj.weight"] = (gq[:, 0].reshape(shape.intermediate, -1), gs[:, 0].reshape(-1))
         quant[p + "mlp.up_proj.weight"] = (gq[:, 1].reshape(shape.intermediate, -1), gs[:, 1].reshape(-1))
         quant[p + "mlp.down_proj.weight"] = (cpu(layer.down.qweight), cpu(layer.down.wscale))
