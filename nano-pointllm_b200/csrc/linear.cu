@@ -1328,12 +1328,17 @@ int launch_linear(const CUtensorMap& tw, const CUtensorMap& tx, LinearArgs& p, c
     p.split = p.clusters = p.red_bufs = 0;
     grid = (int)std::min<long long>(grid_max, p.total_units);
     if (NT >= 128) {
-      // prefill: grouped tile numbering; every full wave but the last runs
-      // whole tiles (one per CTA per wave, no partial-tile fix-up), and the
-      // last one to two waves' worth of tiles are split evenly by stream-K
+      // prefill: grouped tile numbering, whole tiles (one per CTA per wave,
+      // no partial-tile fix-up). With three or more waves every tile runs
+      // whole: a ragged last wave costs less than stream-K's partial tiles,
+      // whose int32 fix-up moves 128 KB of atomics per contribution (config-4
+      // GEMMs on one B200: 1250-1282 us all whole against 1371-1442 with the
+      // last one to two waves split). Two waves: the second is split evenly
+      // by stream-K; fewer tiles than SMs: stream-K over all of them.
       p.raster_g = std::min(kRasterGroup, p.tiles / p.n_tiles);
       const int waves = p.tiles / grid;
-      if (waves >= 2) p.dp_tiles = (waves - 1) * grid;
+      if (waves >= 3) p.dp_tiles = p.tiles;
+      else if (waves == 2) p.dp_tiles = grid;
       p.sk_units = p.total_units - (long long)p.dp_tiles * p.k_blocks;
     }
     p.x_slots = (int)((p.total_units + grid - 1) / grid);

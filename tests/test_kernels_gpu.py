@@ -192,13 +192,14 @@ def _rand_q(gen, *shape):
 
 
 # Prefill tiles (M > 64): 128- and 256-token tiles, two epilogue warpgroups.
-# (120, 40000, 128) and (2100, 8192, 256) have more than two waves of tiles, so
-# whole tiles run data-parallel before the stream-K tail; M = 2100 also has a
-# ragged raster group of token tiles (9 = 8 + 1) and a ragged last token tile.
+# (120, 40000, 128) and (600, 12800, 256) have two waves of tiles: one wave of
+# whole tiles, then stream-K over the rest; (2100, 8192, 256) has three waves
+# (every tile whole), a ragged raster group of token tiles (9 = 8 + 1) and a
+# ragged last token tile.
 LINEAR_SHAPES = [
     (1, 384, 512), (3, 200, 768), (8, 12288, 4096), (8, 4096, 11008), (16, 1000, 512),
     (33, 640, 256), (64, 4096, 4096), (100, 512, 1024), (300, 384, 512), (8, 32003, 4096),
-    (200, 4096, 512), (120, 40000, 128), (2100, 8192, 256),
+    (200, 4096, 512), (120, 40000, 128), (600, 12800, 256), (2100, 8192, 256),
 ]
 
 
